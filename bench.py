@@ -1,0 +1,441 @@
+"""Benchmark of the W4A16 decode hot path on B200 (one JSON line on rank 0).
+
+Workload: all linear layers of one decoded token of a
+Qwen3-8B-shaped model -- 36 decoder layers x {qkv 4096->6144, o 4096->4096,
+gate_up 4096->24576, down 12288->4096}, int4 AWQ, G=128, with distinct weight
+buffers per layer (3.6 GB, far beyond the 126 MB L2, so no flush is needed).
+Within a layer the calls are chained (qkv -> o -> gate_up -> down) through
+row-strided views, as a real decoder would feed them. A step = one token (M=1)
+through all 144 layers, captured once in a CUDA graph and replayed.
+
+Metric: us/token (lower is better). The M=4 figure, per-layer GEMV bandwidth and
+roofline fractions are reported alongside. ``e2e`` repeats the M=1 step through
+the public API with the input copied from pinned host memory and the result
+read back every step.
+
+Multi-GPU (torchrun, N ranks): the same model under tensor parallelism --
+qkv / gate_up column-parallel (N sharded) and o / down row-parallel (K sharded,
+NCCL all-reduce of the partial sums); strong scaling of the same token.
+
+``--impl reference`` times the reference algorithm on the host cores instead
+(the oracle's C restatement of ashqk/ref.py: dequantise in fp32, then the
+GEMM), on a bounded sample extrapolated to the whole token.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "ash-quant-kernels_b200")
+for _p in (ROOT, PKG_DIR):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "us/token all linear layers at M=1,4; GEMV HBM GB/s vs peak; GEMM TFLOPS"
+UNIT = "us/token"
+LAYERS = (("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 24576, 4096), ("down", 4096, 12288))
+N_LAYERS = 36
+GROUP = 128
+FALLBACK_HBM_GBS = 6650.0
+
+
+def w4a16_bytes(m, n, k, g):
+    """Algorithmic bytes of one call (bench/bench_gemm.py:45-46 of the reference)."""
+    return m * k * 2 + k * n // 2 + (k // g) * n * 2 + (k // g) * n // 2 + m * n * 2
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ---------------------------------------------------------------------------
+# CPU reference arm / baseline: the oracle's C restatement of ashqk/ref.py.
+# ---------------------------------------------------------------------------
+
+def cpu_reference_sample(steps: int, warmup: int, budget_s: float | None = None):
+    """Time one decoder layer's four linear calls at M=1 on the host (all threads).
+
+    Returns (us_per_token, threads, sample_description, per_step_us list).
+    """
+    import numpy as np
+
+    from oracle import awq_oracle as O
+
+    threads = O.c_oracle().awq_oracle_threads()
+    probs = [O.make_problem(1, n, k, GROUP, seed=i) for i, (_, n, k) in enumerate(LAYERS)]
+
+    def one_layer_set():
+        t0 = time.perf_counter()
+        for x, qw, qz, s in probs:
+            O.c_gemm(x, qw, qz, s, out_fp16=True)
+        return time.perf_counter() - t0
+
+    for _ in range(warmup):
+        one_layer_set()
+    times = []
+    t_start = time.perf_counter()
+    for i in range(max(steps, 1)):
+        times.append(one_layer_set())
+        if budget_s is not None and time.perf_counter() - t_start > budget_s and i >= 2:
+            break
+    per_token_us = [t * N_LAYERS * 1e6 for t in times]
+    desc = (f"{len(times)} timed samples of one decoder layer's 4 linear calls (qkv, o, gate_up, down) at M=1, "
+            f"G=128, via the C oracle (fp32 dequant + fp64-accumulated GEMM, OpenMP {threads} threads), "
+            f"x36 layers; CPU: {cpu_model()}, os.cpu_count()={os.cpu_count()}")
+    del np
+    return statistics.median(per_token_us), threads, desc, per_token_us
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    value, threads, desc, _ = cpu_reference_sample(args.steps, max(args.warmup, 1))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": max(args.warmup, 1), "ms_per_step": round(value / 1e3, 3),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (fp16 in/out)",
+        "data": "synthetic", "config": workload_config(1),
+        "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(world):
+    return {
+        "workload": "BASELINE config 3: 36-layer Qwen3-8B-shape linear stack (qkv 4096->6144, o 4096->4096, "
+                    "gate_up 4096->24576, down 12288->4096), M=1 (M=4 reported too), int4 AWQ G=128, "
+                    "CUDA-graph replay",
+        "model": "qwen3-8b linear layers (random AWQ weights)",
+        "global_batch": 1, "seq_len": 1,
+        "parallelism": f"tp{world}" if world > 1 else "none",
+        "l2": "inputs larger than L2: 3.6 GB of distinct per-layer weights per step",
+    }
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region (NVML, read-only).
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.01):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._period = period_s
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = None
+            try:
+                import torch
+
+                uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+                self._h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+
+    def _run(self):
+        n = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM))
+                self.reasons |= int(n.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+            except Exception:
+                pass
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        names = [k for k, bit in self.REASONS.items() if self.reasons & bit]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def make_stack(world, rank, device):
+    """Random AWQ weights for 36 layers; TP-sharded when world > 1.
+
+    q, z are uniform over 0..15 (random 32-bit words), scales ~ U(0.002, 0.02),
+    generated on the device from a per-layer seed.
+    """
+    import torch
+
+    gen = torch.Generator(device=device)
+    stack = []
+    for li in range(N_LAYERS):
+        layer = {}
+        for j, (name, n, k) in enumerate(LAYERS):
+            gen.manual_seed(1000 * li + j)
+            col_parallel = name in ("qkv", "gate_up")
+            n_loc = n // world if col_parallel else n
+            k_loc = k // world if not col_parallel else k
+            qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (k_loc, n_loc // 8), dtype=torch.int32, device=device,
+                               generator=gen)
+            qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (k_loc // GROUP, n_loc // 8), dtype=torch.int32,
+                               device=device, generator=gen)
+            s = (torch.rand((k_loc // GROUP, n_loc), device=device, generator=gen) * 0.018 + 0.002).half()
+            layer[name] = (qw, qz, s)
+        stack.append(layer)
+    return stack
+
+
+def stack_step(stack, h, world, group):
+    """One token through every linear layer (public API calls)."""
+    import torch.distributed as dist
+
+    from ashqk import w4a16_linear
+
+    out = None
+    for layer in stack:
+        a = w4a16_linear(h, *layer["qkv"])                      # [M, 6144/P]
+        # Attention output stands in as the first columns of qkv (o input: 4096/P per rank).
+        o_in = a[:, : 4096 // world]
+        b = w4a16_linear(o_in, *layer["o"])                     # partial [M, 4096]
+        if world > 1:
+            dist.all_reduce(b, group=group)
+        c = w4a16_linear(b, *layer["gate_up"])                  # [M, 24576/P]
+        d_in = c[:, : 12288 // world]
+        out = w4a16_linear(d_in, *layer["down"])                # partial [M, 4096]
+        if world > 1:
+            dist.all_reduce(out, group=group)
+    return out
+
+
+def time_graph(graph, steps, warmup, torch, dist, world):
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def per_layer_gemv(stack, m, torch, reps=3):
+    """Average device time of one GEMV launch per layer type (graph of 36 launches
+    over the 36 distinct weight sets, so every launch streams its weights from HBM)."""
+    from ashqk import w4a16_linear
+
+    res = {}
+    for name, n, k in LAYERS:
+        x = torch.randn(m, k, device="cuda").half()
+        w4a16_linear(x, *stack[0][name])
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for layer in stack:
+                w4a16_linear(x, *layer[name])
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(reps):
+            g.replay()
+        end.record()
+        torch.cuda.synchronize()
+        us = start.elapsed_time(end) * 1e3 / (reps * len(stack))
+        nbytes = w4a16_bytes(m, n, k, GROUP)
+        res[name] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1)}
+        del g
+    return res
+
+
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+        group = dist.group.WORLD
+    warmup = max(args.warmup, 3)
+
+    from ashqk import w4a16_linear  # noqa: F401  (loads the extension)
+
+    stack = make_stack(world, rank, device)
+    hbm_peak, peak_kind = load_peaks()
+    results = {}
+    graphs = {}
+    for m in (1, 4):
+        h = torch.randn(m, 4096, device=device).half()
+        stack_step(stack, h, world, group)  # warm-up outside capture (workspaces, NCCL comms)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out = stack_step(stack, h, world, group)
+        graphs[m] = (g, h, out)
+
+    g1, h1, out1 = graphs[1]
+    with ClockSampler(local) as clocks:
+        ms1 = time_graph(g1, args.steps, warmup, torch, dist, world)
+    ms4 = time_graph(graphs[4][0], max(args.steps // 2, 1), warmup, torch, dist, world)
+
+    # End to end through the public API: pinned host input in, result out, every step.
+    h_host = torch.randn(1, 4096).half().pin_memory()
+    y_host = torch.empty(out1.shape, dtype=out1.dtype).pin_memory()
+    for _ in range(warmup):
+        h1.copy_(h_host, non_blocking=True)
+        g1.replay()
+        y_host.copy_(out1, non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        h1.copy_(h_host, non_blocking=True)
+        g1.replay()
+        y_host.copy_(out1, non_blocking=True)
+    end.record()
+    torch.cuda.synchronize()
+    e2e_ms = start.elapsed_time(end) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    d2h_bytes = int(out1.numel()) * out1.element_size()
+    layer_bw = per_layer_gemv(stack, 1, torch) if world == 1 else None
+
+    graphs.clear()
+    del g1, out1
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    per_rank_bytes = sum(w4a16_bytes(1, n // (world if nm in ("qkv", "gate_up") else 1),
+                                     k // (world if nm in ("o", "down") else 1), GROUP)
+                         for nm, n, k in LAYERS) * N_LAYERS
+    stack_gbs = per_rank_bytes / (ms1 * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(ms1 * 1e3, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": warmup, "ms_per_step": round(ms1, 4), "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp16 activations x int4 weights, fp32 accumulate", "data": "synthetic",
+        "config": workload_config(world),
+        "m4_us_per_token": round(ms4 * 1e3 / 4, 1), "m4_us_per_step": round(ms4 * 1e3, 1),
+        "stack_hbm_gbs_per_gpu": round(stack_gbs, 1),
+        "stack_hbm_frac": round(stack_gbs / hbm_peak, 3),
+        "gpu_launches": args.steps * len(LAYERS) * N_LAYERS,
+        "clocks": clocks.summary(),
+        "e2e": {"value": round(e2e_ms * 1e3, 1), "unit": UNIT, "h2d_bytes_per_step": 4096 * 2,
+                "d2h_bytes_per_step": d2h_bytes,
+                "how": "pinned H2D of the token's hidden state + CUDA-graph replay of the 144 "
+                       "public-API w4a16_linear calls + D2H of the last output, CUDA events"},
+    }
+    if layer_bw is not None:
+        tot_bytes = sum(w4a16_bytes(1, n, k, GROUP) for _, n, k in LAYERS)
+        tot_us = sum(layer_bw[nm]["us"] for nm, _, _ in LAYERS)
+        achieved = tot_bytes / tot_us / 1e3
+        line["roofline"] = {
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 3), "peak_kind": peak_kind,
+            "traffic": load_traffic(), "kernel": "gemv_kernel<1,true> (decode GEMV, M=1)",
+            "per_layer": layer_bw,
+        }
+        value, threads, desc, _ = cpu_reference_sample(1000, 1, budget_s=args.cpu_seconds)
+        line["cpu_baseline"] = {"value": round(value, 1), "unit": UNIT, "cores": threads, "kind": "port",
+                                "sample": desc}
+    print(json.dumps(line), flush=True)
+
+
+def load_traffic():
+    """DRAM bytes per GEMV launch from the committed ncu summary, if one exists."""
+    path = os.path.join(ROOT, "profiles", "gemv_decode_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get("bytes_per_launch_stack_avg")
+    except Exception:
+        return None
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU baseline sample")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

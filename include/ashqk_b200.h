@@ -1,0 +1,151 @@
+/*
+ * ashqk_b200.h -- C ABI of the B200 (sm_100a) AWQ W4A16 linear-layer kernels.
+ *
+ * Drop-in for the hot path of MMMchou/ash-quant-kernels (`ashqk`): the same
+ * AutoAWQ "GEMM" tensors, the same math, called with plain pointers and sizes.
+ *
+ *   x        fp16  [M, K]      row stride x_ld (elements), unit column stride
+ *   qweight  int32 [K, N/8]    row stride qw_ld (words); 8 uint4 per word, packed
+ *                              along N in nibble order [0,2,4,6,1,3,5,7]
+ *   qzeros   int32 [K/G, N/8]  row stride qz_ld (words), same packing
+ *   scales   fp16  [K/G, N]    row stride s_ld (elements)
+ *   y        fp16  [M, N]      row stride y_ld (elements), written, never read
+ *   W[k, n] = (q[k, n] - z[k/G, n]) * s[k/G, n];   y = x @ W
+ *
+ * Conventions shared by every entry point:
+ *   - fp16 buffers are passed as `void*` holding IEEE binary16 values;
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); every call is
+ *     asynchronous on it and never synchronises the device;
+ *   - all pointers are device pointers on the current CUDA device;
+ *   - the return value is an ashqk_status; ashqk_status_string() names it.
+ *     On error nothing was launched, except ASHQK_ERR_CUDA, which reports a
+ *     launch failure from the CUDA runtime.
+ *
+ * Workspace. The split-K kernels reduce partial sums through a caller-owned
+ * device workspace of ashqk_*_workspace_size() bytes. It must be zero-filled
+ * once when allocated; every call leaves it zeroed again on exit (the same
+ * self-resetting contract as the reference, ashqk/kernels/w4a16_gemv.py:110-120).
+ * Calls that share a workspace must be ordered on one stream.
+ */
+#ifndef ASHQK_B200_H_
+#define ASHQK_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ASHQK_API __attribute__((visibility("default")))
+#else
+#define ASHQK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum ashqk_status {
+  ASHQK_OK = 0,
+  ASHQK_ERR_INVALID_ARGUMENT = 1, /* a null pointer, a bad size, stride or alignment */
+  ASHQK_ERR_UNSUPPORTED = 2,      /* legal for the format, not handled by this build */
+  ASHQK_ERR_WORKSPACE = 3,        /* workspace missing or smaller than required */
+  ASHQK_ERR_CUDA = 4,             /* the CUDA runtime reported an error */
+  ASHQK_ERR_NO_DEVICE = 5         /* the current device is not an sm_100 GPU */
+} ashqk_status;
+
+/* Static string naming a status code. */
+ASHQK_API const char* ashqk_status_string(int status);
+
+/* Library version, "major.minor.patch". */
+ASHQK_API const char* ashqk_version(void);
+
+/* Largest M the decode GEMV accepts (the dispatcher's GEMV_MAX_M). */
+ASHQK_API int ashqk_gemv_max_m(void);
+
+/*
+ * Bytes of workspace ashqk_w4a16_gemv needs for this problem and split count
+ * (split_k <= 0 picks the default). Replaces the workspace sizing of
+ * ashqk/kernels/w4a16_gemv.py:110-120.
+ */
+ASHQK_API int ashqk_gemv_workspace_size(int M, int N, int K, int group_size, int split_k, size_t* bytes);
+
+/*
+ * Decode GEMV, 1 <= M <= ashqk_gemv_max_m(): y = x @ deq(qweight, qzeros, scales).
+ * Tensor-core (mma.sync m16n8k16) dot products on register-dequantised int4,
+ * per-group factored scales, split-K reduced in the same launch.
+ * split_k <= 0 picks the split from the problem size and SM count.
+ * Replaces ashqk/kernels/w4a16_gemv.py:132-167 (w4a16_gemv).
+ */
+ASHQK_API int ashqk_w4a16_gemv(const void* x, int64_t x_ld, const int32_t* qweight, int64_t qw_ld,
+                     const int32_t* qzeros, int64_t qz_ld, const void* scales, int64_t s_ld,
+                     void* y, int64_t y_ld, int M, int N, int K, int group_size, int split_k,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Selects the decode GEMV kernel for later calls in this process: 0 = automatic
+ * (the TMA-pipelined kernel whenever N % 32 == 0 and qweight rows are 16-byte
+ * aligned, else the register-streaming kernel), 1 = always the
+ * register-streaming kernel, 2 = always the TMA kernel (ineligible problems
+ * then return ASHQK_ERR_UNSUPPORTED). No reference counterpart: a test and
+ * tuning switch.
+ */
+ASHQK_API int ashqk_set_gemv_kernel(int which);
+
+/*
+ * Reads (and with clear != 0 resets) the device error word of the current
+ * device after synchronising it. Bit 1: a pipeline wait inside a kernel ran
+ * past its time limit and the kernel gave up (its output and any split-K
+ * workspace it used are then invalid; re-zero the workspace). Bit 2: a kernel
+ * rejected its launch parameters. No reference counterpart.
+ */
+ASHQK_API int ashqk_get_device_errors(unsigned int* bits, int clear);
+
+/*
+ * Bytes of workspace ashqk_w4a16_gemm needs (0 today: the prefill GEMM does not
+ * split K). Replaces the sizing of ashqk/kernels/w4a16_gemm_v3.py:108-119.
+ */
+ASHQK_API int ashqk_gemm_workspace_size(int M, int N, int K, int group_size, size_t* bytes);
+
+/*
+ * Prefill GEMM, any M >= 1: y = x @ deq(...). int4 is dequantised into shared
+ * memory and fed to tcgen05.mma with the accumulator in tensor memory.
+ * Replaces ashqk/kernels/w4a16_gemm_v3.py:131-171 (w4a16_gemm_v3).
+ */
+ASHQK_API int ashqk_w4a16_gemm(const void* x, int64_t x_ld, const int32_t* qweight, int64_t qw_ld,
+                     const int32_t* qzeros, int64_t qz_ld, const void* scales, int64_t s_ld,
+                     void* y, int64_t y_ld, int M, int N, int K, int group_size,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Workspace for ashqk_w4a16_linear: the larger of the two paths' needs.
+ */
+ASHQK_API int ashqk_linear_workspace_size(int M, int N, int K, int group_size, size_t* bytes);
+
+/*
+ * Dispatcher: M <= ashqk_gemv_max_m() runs the GEMV, larger M the GEMM.
+ * Replaces ashqk/ops.py:18-26 (w4a16_linear) for a 2-D x.
+ */
+ASHQK_API int ashqk_w4a16_linear(const void* x, int64_t x_ld, const int32_t* qweight, int64_t qw_ld,
+                       const int32_t* qzeros, int64_t qz_ld, const void* scales, int64_t s_ld,
+                       void* y, int64_t y_ld, int M, int N, int K, int group_size,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * W = (q - z) * s written as fp16 [K, N] (row stride w_ld), bit-identical to
+ * dequantize_awq(qweight, qzeros, scales, torch.float16) of ashqk/ref.py:78-86.
+ */
+ASHQK_API int ashqk_dequantize_awq_f16(const int32_t* qweight, int64_t qw_ld, const int32_t* qzeros,
+                             int64_t qz_ld, const void* scales, int64_t s_ld, void* w, int64_t w_ld,
+                             int N, int K, int group_size, void* stream);
+
+/*
+ * Same, written as fp32 [K, N]: dequantize_awq(..., torch.float32) of ashqk/ref.py:78-86.
+ */
+ASHQK_API int ashqk_dequantize_awq_f32(const int32_t* qweight, int64_t qw_ld, const int32_t* qzeros,
+                             int64_t qz_ld, const void* scales, int64_t s_ld, float* w, int64_t w_ld,
+                             int N, int K, int group_size, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ASHQK_B200_H_ */

@@ -1,0 +1,66 @@
+"""The C-ABI library (include/ashqk_b200.h) loads and exports every declared symbol.
+
+CPU-only: no call here launches a kernel. Argument validation that happens
+before any CUDA call is checked through ctypes.
+"""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "ashqk_b200.h")
+LIB = os.path.join(ROOT, "ash-quant-kernels_b200", "ashqk", "libashqk_b200.so")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"ASHQK_API\s+[\w\s\*]+?\b(ashqk_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(LIB):
+        pytest.fail(f"{LIB} not built; run python ash-quant-kernels_b200/build.py")
+    return ctypes.CDLL(LIB)
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    for required in ("ashqk_w4a16_linear", "ashqk_w4a16_gemv", "ashqk_w4a16_gemm", "ashqk_dequantize_awq_f16",
+                     "ashqk_dequantize_awq_f32", "ashqk_status_string"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [n for n in declared_symbols() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_status_strings_and_version(lib):
+    lib.ashqk_status_string.restype = ctypes.c_char_p
+    lib.ashqk_version.restype = ctypes.c_char_p
+    assert lib.ashqk_status_string(0) == b"ok"
+    assert b"invalid" in lib.ashqk_status_string(1)
+    assert b"unknown" in lib.ashqk_status_string(999)
+    assert re.fullmatch(rb"\d+\.\d+\.\d+", lib.ashqk_version())
+    assert lib.ashqk_gemv_max_m() == 16
+
+
+def test_invalid_arguments_rejected_before_launch(lib):
+    f = lib.ashqk_w4a16_linear
+    vp, i64, ci = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    f.argtypes = [vp, i64, vp, i64, vp, i64, vp, i64, vp, i64, ci, ci, ci, ci, vp, ctypes.c_size_t, vp]
+    fake = ctypes.c_void_p(0x1000)  # never dereferenced: validation fails first
+    # null x
+    assert f(None, 256, fake, 8, fake, 8, fake, 64, fake, 64, 1, 64, 256, 128, None, 0, None) == 1
+    # N not a multiple of 8
+    assert f(fake, 256, fake, 8, fake, 8, fake, 60, fake, 60, 1, 60, 256, 128, None, 0, None) == 1
+    # K not a multiple of the group size
+    assert f(fake, 250, fake, 8, fake, 8, fake, 64, fake, 64, 1, 64, 250, 128, None, 0, None) == 1
+    # leading dimension smaller than the row
+    assert f(fake, 100, fake, 8, fake, 8, fake, 64, fake, 64, 1, 64, 256, 128, None, 0, None) == 1
+    sz = ctypes.c_size_t(0)
+    assert lib.ashqk_linear_workspace_size(1, 60, 256, 128, ctypes.byref(sz)) == 1
