@@ -45,6 +45,17 @@ __device__ __forceinline__ void zero_consts(uint32_t zw, uint32_t (&zc)[8]) {
   }
 }
 
+// Magic-number halves without the zero-point subtraction: slots 0 and 2 hold
+// 1024 + q (low nibbles), slots 1 and 3 hold 1024 + 16 q (high nibbles). Dot
+// products of these with x are corrected once per group (see gemv_tma.cu).
+__device__ __forceinline__ void unpack_raw(uint32_t T, uint32_t (&o)[4]) {
+  const uint32_t T8 = T >> 8;
+  o[0] = lop3_and_or(T, kLoNibbles, kMagic1024x2);
+  o[1] = lop3_and_or(T, kHiNibbles, kMagic1024x2);
+  o[2] = lop3_and_or(T8, kLoNibbles, kMagic1024x2);
+  o[3] = lop3_and_or(T8, kHiNibbles, kMagic1024x2);
+}
+
 // Slot of column j (0..7 of a word) in the unpack_pairs output of T_a / T_b.
 __device__ __forceinline__ constexpr int col_slot(int j) { return 4 * (j >> 2) + (((j & 1) << 1) | ((j >> 1) & 1)); }
 

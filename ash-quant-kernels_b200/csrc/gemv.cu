@@ -398,9 +398,13 @@ int gemv_launch_rows(const __half* x, int64_t x_ld, const int32_t* qw, int64_t q
   if (G % 16) return ASHQK_ERR_UNSUPPORTED;
   const bool tma_ok = gemv_tma_eligible(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, M, N, G);
   if (g_gemv_impl == 2 && !tma_ok) return ASHQK_ERR_UNSUPPORTED;
-  if (tma_ok && g_gemv_impl != 1)
-    return gemv_tma_launch(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G, split_k, workspace, ws_bytes,
-                           info.sm_count, stream);
+  if (tma_ok && g_gemv_impl != 1) {
+    const int rc_tma = gemv_tma_launch(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G, split_k, workspace,
+                                       ws_bytes, info.sm_count, stream);
+    // A slice that cannot fit the TMA kernel's shared memory (tiny groups with a
+    // forced small split) falls back to the register-streaming kernel.
+    if (!(rc_tma == ASHQK_ERR_UNSUPPORTED && g_gemv_impl == 0)) return rc_tma;
+  }
   Plan p;
   plan_gemv(M, N, K, G, split_k, info.sm_count, &p);
   if (p.smem > 200 * 1024 || p.tiles > kMaxTiles) return ASHQK_ERR_UNSUPPORTED;

@@ -42,13 +42,26 @@ constexpr int kConsumers = 32 * kConsumerWarps;
 constexpr int kThreads = kConsumers + 32;
 constexpr int kTileWords = 32;  // one 128-byte TMA row
 constexpr int kTileCols = kTileWords * 8;
-constexpr int kStageRows = 64;
-constexpr int kStageBytes = kStageRows * kTileWords * 4;
-constexpr int kStages = 8;
+// A stage is kBoxes TMA boxes of 64 rows x 128 bytes behind one mbarrier phase:
+// the barrier round trip is paid once per kBoxes x 8 KB of weights.
+#ifndef ASHQK_GEMV_BOXES
+#define ASHQK_GEMV_BOXES 2
+#endif
+#ifndef ASHQK_GEMV_STAGES
+#define ASHQK_GEMV_STAGES 6
+#endif
+constexpr int kBoxRows = 64;
+constexpr int kBoxBytes = kBoxRows * kTileWords * 4;
+constexpr int kBoxes = ASHQK_GEMV_BOXES;
+constexpr int kStageRows = kBoxRows * kBoxes;
+constexpr int kStageBytes = kBoxBytes * kBoxes;
+constexpr int kStages = ASHQK_GEMV_STAGES;
+static_assert(kBoxes == 1 || kBoxes % 2 == 0, "stages hold one box or an even number of boxes");
 constexpr int kMaxTiles = 16384;
 constexpr int kMaxCluster = 16;
 constexpr size_t kCounterBytes = kMaxTiles * sizeof(int);
-constexpr size_t kSmemLimit = 110 * 1024;  // two CTAs per SM
+constexpr size_t kSmemLimitTwoCtas = 112 * 1024;  // M <= 8: two CTAs per SM
+constexpr size_t kSmemLimitOneCta = 220 * 1024;   // M > 8: one CTA per SM (register bound)
 
 struct TmaGemvArgs {
   const __half* x;
@@ -64,10 +77,11 @@ struct TmaGemvArgs {
   int splits;
   int x_stride;      // halves; == 8 mod 64 for conflict-free fragment reads
   int max_groups;
+  int spin;          // producer polls instead of sleeping on the empty barriers
 };
 
 template <int MT, bool CLUSTER>
-__global__ void __launch_bounds__(kThreads, MT == 1 ? 2 : 1) gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap,
+__global__ void __launch_bounds__(kThreads) __maxnreg__(MT == 1 ? 112 : 168) gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap,
                                                                const TmaGemvArgs a) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
@@ -130,11 +144,15 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 2 : 1) gemv_tma_kernel(con
         bulk_load(zs + gi * kTileWords, a.qz + static_cast<int64_t>(g0 + gi) * a.qz_ld + tile * kTileWords,
                   cols_valid / 2, aux_bar);
       }
+      auto issue = [&](int i, int slot) {
+        mbar_arrive_expect_tx(&full[slot], kStageBytes);
+#pragma unroll
+        for (int b = 0; b < kBoxes; ++b)
+          tma_load_2d(ring + slot * kStageBytes + b * kBoxBytes, &tmap, tile * kTileWords,
+                      (st0 + i) * kStageRows + b * kBoxRows, &full[slot]);
+      };
       const int prologue = min(nst, kStages);
-      for (int i = 0; i < prologue; ++i) {
-        mbar_arrive_expect_tx(&full[i], kStageBytes);
-        tma_load_2d(ring + i * kStageBytes, &tmap, tile * kTileWords, (st0 + i) * kStageRows, &full[i]);
-      }
+      for (int i = 0; i < prologue; ++i) issue(i, i);
       // x is the previous kernel's output.
       pdl_wait();
       mbar_arrive_expect_tx(x_bar, static_cast<uint32_t>(a.M) * krows * 2);
@@ -143,9 +161,8 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 2 : 1) gemv_tma_kernel(con
       int issued = prologue;
       for (int i = prologue; i < nst; ++i) {
         const int slot = i % kStages;
-        if (!mbar_wait(&empty[slot], ((i / kStages) - 1) & 1, &abort_flag)) break;
-        mbar_arrive_expect_tx(&full[slot], kStageBytes);
-        tma_load_2d(ring + slot * kStageBytes, &tmap, tile * kTileWords, (st0 + i) * kStageRows, &full[slot]);
+        if (!mbar_wait(&empty[slot], ((i / kStages) - 1) & 1, &abort_flag, a.spin != 0)) break;
+        issue(i, slot);
         ++issued;
       }
       if (abort_flag) {
@@ -176,6 +193,7 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 2 : 1) gemv_tma_kernel(con
       }
     }
     bool ok = mbar_wait(aux_bar, 0, &abort_flag) && mbar_wait(x_bar, 0, &abort_flag);
+
     named_barrier_sync(1, kConsumers);
 
     float part[MT][4][4];
@@ -185,10 +203,10 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 2 : 1) gemv_tma_kernel(con
       for (int j = 0; j < 4; ++j)
 #pragma unroll
         for (int r = 0; r < 4; ++r) part[mt][j][r] = 0.f;
-    uint32_t zc[8];
-    uint32_t sh[4];                       // this lane's 8 scales of the current group (half2)
-    const int wcol = cw * 8 + g;          // the word (8 columns) of the tile this lane unpacks
-    const int chunk = wcol >> 2;          // its 16-byte chunk in a 128-byte row
+    uint32_t zc[8];                        // zero-point constants of this lane's word (current group)
+    uint32_t sh[4];                        // its 8 scales, as half2
+    const int wcol = cw * 8 + g;           // the word (8 columns) of the tile this lane unpacks
+    const int chunk = wcol >> 2;           // its 16-byte chunk in a 128-byte row
     const int in_chunk = (wcol & 3) * 4;
     const uint32_t ring_s = smem_u32(ring);
     const uint32_t ss_s = smem_u32(ss);
@@ -212,7 +230,9 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 2 : 1) gemv_tma_kernel(con
     }
     int grp = -1, grp_end = -1;
 
-    auto flush = [&]() {
+    // part accumulates sum_k x_k (q_k - z) over the current group; the scale is
+    // applied once per group in fp32.
+    auto flush = [&](int) {
       float sc[8];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -241,43 +261,91 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 2 : 1) gemv_tma_kernel(con
       sh[3] = sv.w;
     };
 
+    // One 16-row step: unpack 4 rows x 8 columns and feed 4 (x MT) mma.sync.
+    auto step = [&](const uint32_t (&w)[4], const uint32_t (&b)[MT][2]) {
+      const uint32_t za[4] = {zc[0], zc[1], zc[2], zc[3]};
+      const uint32_t zb[4] = {zc[4], zc[5], zc[6], zc[7]};
+      uint32_t oa[4], ob[4], oc[4], od[4];
+      unpack_pairs(prmt(w[0], w[1], 0x6420u), za, oa);
+      unpack_pairs(prmt(w[0], w[1], 0x7531u), zb, ob);
+      unpack_pairs(prmt(w[2], w[3], 0x6420u), za, oc);
+      unpack_pairs(prmt(w[2], w[3], 0x7531u), zb, od);
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int sl = ((j & 1) << 1) | (j >> 1);
+          const uint32_t A[4] = {oa[sl], ob[sl], oc[sl], od[sl]};
+          mma_16816(part[mt][j], A, b[mt][0], b[mt][1]);
+        }
+    };
+    auto load_x = [&](uint32_t off, uint32_t (&b)[MT][2]) {
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        b[mt][0] = xok[mt] ? lds_u32(xa[mt] + off) : 0u;
+        b[mt][1] = xok[mt] ? lds_u32(xa[mt] + off + 16) : 0u;
+      }
+    };
+    auto enter_group = [&](int k0) {
+      if (k0 >= grp_end) {
+        if (grp >= 0) flush(grp - g0);
+        grp = k0 / a.G;
+        grp_end = (grp + 1) * a.G;
+        load_group(grp - g0);
+      }
+    };
+    // The warp's two steps share one quantization group whenever G % 32 == 0.
+    const bool pair_groups = (a.G % 32) == 0;
+
     for (int i = 0; ok && i < nst; ++i) {
-      const int slot = i & (kStages - 1);
+      const int slot = i % kStages;
       if (!mbar_wait(&full[slot], (i / kStages) & 1, &abort_flag)) break;
-      const uint32_t st = ring_s + slot * kStageBytes;
-      const uint32_t xoff = static_cast<uint32_t>(i) * (kStageRows * 2);
+      const int k_stage = k_begin + kStageRows * i;
+      if (pair_groups && k_stage + kStageRows <= k_end) {
+        // Fast path (every box of the stage valid): shared loads are issued two
+        // boxes at a time ahead of their unpack / mma chains, so one wait on the
+        // stage covers the latency of the next loads (the barrier's memory
+        // clobber would otherwise serialise them box by box).
+        constexpr int kBatch = kBoxes >= 2 ? 2 : 1;
 #pragma unroll
-      for (int s2 = 0; s2 < 2; ++s2) {
-        const int k0 = k_begin + kStageRows * i + 32 * kh + 16 * s2;
-        if (k0 < k_end) {
-          if (k0 >= grp_end) {  // first step of a new quantization group
-            if (grp >= 0) flush();
-            grp = k0 / a.G;
-            grp_end = (grp + 1) * a.G;
-            load_group(grp - g0);
-          }
-          uint32_t w[4];
+        for (int bp = 0; bp < kBoxes; bp += kBatch) {
+          uint32_t w[kBatch][2][4], b[kBatch][2][MT][2];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) w[q] = lds_u32(st + roff[q] + s2 * 2048);
-          const uint32_t za[4] = {zc[0], zc[1], zc[2], zc[3]};
-          const uint32_t zb[4] = {zc[4], zc[5], zc[6], zc[7]};
-          uint32_t oa[4], ob[4], oc[4], od[4];
-          unpack_pairs(prmt(w[0], w[1], 0x6420u), za, oa);
-          unpack_pairs(prmt(w[0], w[1], 0x7531u), zb, ob);
-          unpack_pairs(prmt(w[2], w[3], 0x6420u), za, oc);
-          unpack_pairs(prmt(w[2], w[3], 0x7531u), zb, od);
+          for (int u = 0; u < kBatch; ++u) {
+            const uint32_t st = ring_s + slot * kStageBytes + (bp + u) * kBoxBytes;
+            const uint32_t xoff = static_cast<uint32_t>(i * kStageRows + (bp + u) * kBoxRows) * 2;
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-            uint32_t b0 = 0u, b1 = 0u;
-            if (xok[mt]) {
-              b0 = lds_u32(xa[mt] + xoff + s2 * 32);
-              b1 = lds_u32(xa[mt] + xoff + s2 * 32 + 16);
+            for (int q = 0; q < 4; ++q) {
+              w[u][0][q] = lds_u32(st + roff[q]);
+              w[u][1][q] = lds_u32(st + roff[q] + 2048);
             }
+            load_x(xoff, b[u][0]);
+            load_x(xoff + 32, b[u][1]);
+          }
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int sl = ((j & 1) << 1) | (j >> 1);
-              const uint32_t A[4] = {oa[sl], ob[sl], oc[sl], od[sl]};
-              mma_16816(part[mt][j], A, b0, b1);
+          for (int u = 0; u < kBatch; ++u) {
+            enter_group(k_stage + (bp + u) * kBoxRows + 32 * kh);
+            step(w[u][0], b[u][0]);
+            step(w[u][1], b[u][1]);
+          }
+        }
+      } else {
+        // Ragged tail, or G not a multiple of 32: one step at a time.
+#pragma unroll 1
+        for (int bx = 0; bx < kBoxes; ++bx) {
+          const uint32_t st = ring_s + slot * kStageBytes + bx * kBoxBytes;
+          const uint32_t xoff = static_cast<uint32_t>(i * kStageRows + bx * kBoxRows) * 2;
+          const int kb = k_stage + kBoxRows * bx + 32 * kh;
+#pragma unroll
+          for (int s2 = 0; s2 < 2; ++s2) {
+            const int k0 = kb + 16 * s2;
+            if (k0 < k_end) {
+              enter_group(k0);
+              uint32_t w[4], b[MT][2];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) w[q] = lds_u32(st + roff[q] + s2 * 2048);
+              load_x(xoff + s2 * 32, b);
+              step(w, b);
             }
           }
         }
@@ -285,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 2 : 1) gemv_tma_kernel(con
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
-    if (grp >= 0) flush();
+    if (grp >= 0) flush(grp - g0);
   }
 
   // ---------------- CTA partial tile ----------------
@@ -362,6 +430,14 @@ struct TmaPlan {
   size_t smem, ws_bytes;
 };
 
+bool producer_spin_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("ASHQK_GEMV_SPIN");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 int ctas_per_sm_target() {
   static const int v = [] {
     const char* e = std::getenv("ASHQK_GEMV_CTAS_PER_SM");
@@ -397,7 +473,7 @@ void plan_tma(int M, int N, int K, int G, int split_req, int sm_count, TmaPlan* 
     p->smem = 1024 /* alignment slack */ + static_cast<size_t>(kStages) * kStageBytes +
               static_cast<size_t>(M) * p->x_stride * 2 + static_cast<size_t>(p->max_groups) * kTileCols * 2 +
               static_cast<size_t>(p->max_groups) * kTileWords * 4 + (2 * kStages + 2) * 8;
-    if (p->smem <= kSmemLimit || splits >= p->stages_total) break;
+    if (p->smem <= (M > 8 ? kSmemLimitOneCta : kSmemLimitTwoCtas) || splits >= p->stages_total) break;
   }
   p->cluster = use_cluster_reduction() && p->splits > 1 && p->splits <= kMaxCluster;
   p->ws_bytes = (p->splits > 1 && !p->cluster)
@@ -412,7 +488,7 @@ int launch_tma(const CUtensorMap& map, const TmaGemvArgs& args, const TmaPlan& p
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ASHQK_ERR_CUDA;
   auto kernel = gemv_tma_kernel<MT, CLUSTER>;
   if (!configured[dev]) {
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit) != cudaSuccess ||
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimitOneCta) != cudaSuccess ||
         cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared) != cudaSuccess)
       return ASHQK_ERR_CUDA;
@@ -464,12 +540,12 @@ int gemv_tma_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw
                     void* workspace, size_t ws_bytes, int sm_count, cudaStream_t stream) {
   TmaPlan p;
   plan_tma(M, N, K, G, split_k, sm_count, &p);
-  if (p.smem > kSmemLimit || p.tiles > kMaxTiles) return ASHQK_ERR_UNSUPPORTED;
+  if (p.smem > (M > 8 ? kSmemLimitOneCta : kSmemLimitTwoCtas) || p.tiles > kMaxTiles) return ASHQK_ERR_UNSUPPORTED;
   if (p.ws_bytes > 0 && (workspace == nullptr || ws_bytes < p.ws_bytes || !aligned(workspace, 256)))
     return ASHQK_ERR_WORKSPACE;
   CUtensorMap map;
   int rc = encode_tensor_map_2d(&map, CU_TENSOR_MAP_DATA_TYPE_INT32, const_cast<int32_t*>(qw), N / 8, K,
-                                static_cast<uint64_t>(qw_ld) * 4, kTileWords, kStageRows,
+                                static_cast<uint64_t>(qw_ld) * 4, kTileWords, kBoxRows,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   TmaGemvArgs a;
@@ -490,6 +566,7 @@ int gemv_tma_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw
   a.splits = p.splits;
   a.x_stride = p.x_stride;
   a.max_groups = p.max_groups;
+  a.spin = producer_spin_enabled() ? 1 : 0;
   if (p.ws_bytes > 0) {
     a.counters = static_cast<int*>(workspace);
     a.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);

@@ -84,11 +84,13 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 // Bounded wait for the phase with the given parity. Returns false (and flags
 // the device error word) if the limit ran out, or if `abort` was already set by
 // another thread of the CTA; on false the caller must stop its pipeline work.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// `spin` polls without the suspend hint: lower wake-up latency, for the single
+// producer thread whose refills gate the pipeline.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, bool spin = false) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
+    if (spin ? mbar_try_wait(bar, parity) : mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
     if (*abort) return false;
     if (clock64() - t0 > kWaitLimitCycles) {
       *abort = 1;

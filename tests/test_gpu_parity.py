@@ -206,7 +206,13 @@ def test_gemv_kernels_agree(m, n, k, group_size, gemv_kernel):
     y_true = O.c_gemm(x, qw, qz, s)
     e_cublas = _cublas_err(x, qw, qz, s, y_true)
     for split in (0, 1, 3):
-        y = w4a16_gemv(*to_cuda(x, qw, qz, s), {"split_k": split})
+        try:
+            y = w4a16_gemv(*to_cuda(x, qw, qz, s), {"split_k": split})
+        except RuntimeError as err:
+            # Forcing the TMA kernel on a slice whose 16-row groups do not fit its
+            # shared memory is reported as unsupported (auto mode falls back).
+            assert gemv_kernel == 2 and group_size < 32 and "unsupported" in str(err), err
+            continue
         assert rel_err(y, y_true) <= 2 * e_cublas + 1e-5, split
 
 
