@@ -81,6 +81,26 @@ ASHQK_API int ashqk_w4a16_gemv(const void* x, int64_t x_ld, const int32_t* qweig
                      void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Decode GEMV that allocates nothing: same arguments and result as
+ * ashqk_w4a16_gemv, but without a workspace. It is meant for callers that
+ * cannot allocate device memory (a plugin that is handed only device pointers
+ * by its host framework, or a caller that must not call cudaMalloc on its hot
+ * path). The split-K scratch is a fixed 8 MiB array inside this library, held
+ * on every GPU that loads it until the process exits; problems whose scratch
+ * need exceeds it (ashqk_gemv_workspace_size() > 8 MiB) return
+ * ASHQK_ERR_WORKSPACE without launching anything. The first call on a device
+ * looks up that array's device address, so make it before any stream capture.
+ * All calls share the array: calls that may overlap on the GPU (other
+ * streams, other threads) race, so order them on one stream. Each call clears
+ * the part that must start at zero. This entry point has no counterpart in the
+ * reference.
+ */
+ASHQK_API int ashqk_w4a16_gemv_noalloc(const void* x, int64_t x_ld, const int32_t* qweight, int64_t qw_ld,
+                                       const int32_t* qzeros, int64_t qz_ld, const void* scales, int64_t s_ld,
+                                       void* y, int64_t y_ld, int M, int N, int K, int group_size, int split_k,
+                                       void* stream);
+
+/*
  * Selects the decode GEMV kernel for later calls in this process: 0 = automatic
  * (the TMA-pipelined kernel whenever N % 32 == 0 and qweight rows are 16-byte
  * aligned, else the register-streaming kernel), 1 = always the
