@@ -373,8 +373,16 @@ int gemv_tma_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw
                     const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K, int G, int split_k,
                     void* workspace, size_t ws_bytes, int sm_count, cudaStream_t stream);
 
+bool gemv_strip_eligible(const void* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
+                         int64_t qz_ld, const void* s, int64_t s_ld, int M, int N, int G);
+int gemv_strip_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
+                      int64_t qz_ld, const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K, int G,
+                      int sm_count, cudaStream_t stream);
+
 namespace {
-int g_gemv_impl = 0;  // 0 auto, 1 register-streaming kernel, 2 TMA-pipelined kernel
+// 0 auto (column strips, then split-K TMA, then register streaming),
+// 1 register-streaming, 2 split-K TMA, 3 column strips.
+int g_gemv_impl = 0;
 }
 
 int gemv_workspace_bytes(int M, int N, int K, int G, int split_k, size_t* bytes) {
@@ -396,6 +404,15 @@ int gemv_launch_rows(const __half* x, int64_t x_ld, const int32_t* qw, int64_t q
   int rc = device_info(&info);
   if (rc) return rc;
   if (G % 16) return ASHQK_ERR_UNSUPPORTED;
+  // Column strips need no workspace; a forced split_k asks for a K split, so it
+  // goes to the split-K kernels.
+  const bool strip_ok = gemv_strip_eligible(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, M, N, G);
+  if (g_gemv_impl == 3 && !strip_ok) return ASHQK_ERR_UNSUPPORTED;
+  if (strip_ok && (g_gemv_impl == 3 || (g_gemv_impl == 0 && split_k <= 0))) {
+    const int rc_strip = gemv_strip_launch(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G,
+                                           info.sm_count, stream);
+    if (!(rc_strip == ASHQK_ERR_UNSUPPORTED && g_gemv_impl == 0)) return rc_strip;
+  }
   const bool tma_ok = gemv_tma_eligible(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, M, N, G);
   if (g_gemv_impl == 2 && !tma_ok) return ASHQK_ERR_UNSUPPORTED;
   if (tma_ok && g_gemv_impl != 1) {
@@ -453,7 +470,7 @@ int gemv_max_m() { return kMaxM; }
 extern "C" int ashqk_gemv_max_m(void) { return ashqk::kMaxM; }
 
 extern "C" int ashqk_set_gemv_kernel(int which) {
-  if (which < 0 || which > 2) return ASHQK_ERR_INVALID_ARGUMENT;
+  if (which < 0 || which > 3) return ASHQK_ERR_INVALID_ARGUMENT;
   ashqk::g_gemv_impl = which;
   return ASHQK_OK;
 }

@@ -1,0 +1,458 @@
+// Decode GEMV for AWQ W4A16 (M <= 16): column strips with the whole K per CTA.
+//
+// Same math as the other decode kernels (reference ashqk/kernels/w4a16_gemv.py:28-107):
+// y = x @ W, W = (q - z) * s, factored per quantization group, fp32 accumulation.
+//
+// Why this shape: on 2-10 us layers the split-K variants spend as long in their
+// prologue (staging x, scales, zeros) and their split-K tail (partial sums to
+// global memory, fence, arrival counter, a last CTA re-reading them) as in
+// streaming weights. Here a CTA owns 64 output columns over all of K, so there
+// is no split-K tail at all, and everything a stage needs -- 256 rows of packed
+// weights (a 32-byte wide TMA box), the matching 256 columns of x, and the
+// scale / zero rows of the groups it spans -- arrives with one mbarrier phase,
+// so there is no prologue either. Many stages (up to ~200 KB) are kept in
+// flight per SM: a 64 KB ring lets one SM stream ~49 GB/s, and layers with few
+// column strips need more than that per SM.
+//
+// Warps: one producer (lane 0 issues all TMA loads) and C consumer warps. Stage
+// i belongs to consumer warp i % C, which runs all 16 of its 16-row steps with
+// no further synchronisation and keeps one quantization group for G/16 steps.
+// A lane unpacks one word (8 columns) of rows {2t, 2t+1, 2t+8, 2t+9} per step
+// -- the k order of an mma.sync A fragment -- with the prmt / LOP3 / HSUB2 code
+// of csrc/awq_unpack.cuh, and mma.sync.m16n8k16 accumulates sum x (q - z) per
+// group in fp32; the scale is applied once per group. At the end the C warps'
+// partial tiles are summed in shared memory and y is stored.
+//
+// Programmatic dependent launch: weights, scales and zeros of the first ring
+// stages are requested before griddepcontrol.wait; x (the previous kernel's
+// output) after it; y is written only after it.
+#include <algorithm>
+#include <cstdlib>
+
+#include "awq_unpack.cuh"
+#include "sm100.cuh"
+
+namespace ashqk {
+namespace {
+
+constexpr int kStripCols = 64;
+constexpr int kStripWords = kStripCols / 8;
+constexpr int kBoxRows = 256;                            // rows per stage (TMA box height limit)
+constexpr int kWeightBytes = kBoxRows * kStripWords * 4;  // 8 KB
+constexpr int kXRowBytes = kBoxRows * 2;                  // one token's 256 x values
+constexpr int kMaxStages = 24;
+
+struct StripArgs {
+  __half* y;
+  int64_t y_ld;
+  int M, N, K, G;
+  int stages_total;  // ceil(K / 256)
+  int ksplit;        // CTAs (one thread-block cluster) sharing a strip's K range
+  int ring;          // stages resident in shared memory
+  int gps;           // scale / zero rows loaded per stage
+  int stage_bytes;   // bytes of one ring slot (multiple of 128)
+  int x_off, s_off, z_off;  // byte offsets of x, scales, zeros inside a slot
+  uint32_t tx_bytes;        // transaction bytes per stage
+};
+
+struct StripMaps {
+  CUtensorMap qw, x, s, z;
+};
+
+template <int MT, int C>
+__global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_constant__ StripMaps maps,
+                                                                  const StripArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full[kMaxStages];
+  __shared__ uint64_t empty[kMaxStages];
+  __shared__ int abort_flag;
+
+  const int strip = blockIdx.x;
+  const int col0 = strip * kStripCols;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  // This CTA's stages of the strip's K range (blockIdx.y of a.ksplit).
+  const int sb = static_cast<int>(static_cast<int64_t>(blockIdx.y) * a.stages_total / a.ksplit);
+  const int se = static_cast<int>(static_cast<int64_t>(blockIdx.y + 1) * a.stages_total / a.ksplit);
+  const int nloc = se - sb;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.ring; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  float acc[MT][4][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[mt][j][r] = 0.f;
+
+  if (warp == C) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      prefetch_tensormap(&maps.qw);
+      prefetch_tensormap(&maps.x);
+      prefetch_tensormap(&maps.s);
+      prefetch_tensormap(&maps.z);
+      auto issue_weights = [&](int i, int slot) {
+        unsigned char* base = smem + slot * a.stage_bytes;
+        const int k0 = i * kBoxRows;
+        mbar_arrive_expect_tx(&full[slot], a.tx_bytes);
+        tma_load_2d(base, &maps.qw, strip * kStripWords, k0, &full[slot]);
+        tma_load_2d(base + a.s_off, &maps.s, col0, k0 / a.G, &full[slot]);
+        tma_load_2d(base + a.z_off, &maps.z, strip * kStripWords, k0 / a.G, &full[slot]);
+      };
+      auto issue_x = [&](int i, int slot) {
+        tma_load_2d(smem + slot * a.stage_bytes + a.x_off, &maps.x, i * kBoxRows, 0, &full[slot]);
+      };
+      const int prologue = min(nloc, a.ring);
+      for (int li = 0; li < prologue; ++li) issue_weights(sb + li, li);
+      pdl_wait();  // x is the previous kernel's output
+      for (int li = 0; li < prologue; ++li) issue_x(sb + li, li);
+      int issued = prologue;
+      for (int li = prologue; li < nloc; ++li) {
+        const int slot = li % a.ring;
+        if (!mbar_wait(&empty[slot], ((li / a.ring) - 1) & 1, &abort_flag)) break;
+        issue_weights(sb + li, slot);
+        issue_x(sb + li, slot);
+        ++issued;
+      }
+      if (abort_flag) {
+        int unused = 0;
+        for (int slot = 0; slot < a.ring && slot < issued; ++slot)
+          mbar_wait(&full[slot], ((issued - 1 - slot) / a.ring) & 1, &unused);
+      }
+    }
+  } else {
+    // ---------------- consumers ----------------
+    pdl_wait();  // y may only be written after the previous kernel ends
+    const int g = lane >> 2;
+    const int t = lane & 3;
+    const uint32_t smem_s = smem_u32(smem);
+    // Row offsets (bytes) of rows {2t, 2t+1, 2t+8, 2t+9} of step 0, word g.
+    uint32_t roff[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) roff[q] = (2 * t + (q & 1) + 8 * (q >> 1)) * (kStripWords * 4) + 4 * g;
+    bool xok[MT];
+    uint32_t xrow[MT];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      xok[mt] = 8 * mt + g < a.M;
+      xrow[mt] = (xok[mt] ? 8 * mt + g : 0) * kXRowBytes + 4 * t;
+    }
+    float part[MT][4][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) part[mt][j][r] = 0.f;
+    uint32_t zc[8];
+    uint32_t sh[4];
+    int cur_grp = -1;
+
+    auto flush = [&]() {
+      float sc[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(u32_as_h2(sh[i]));
+        sc[2 * i] = f.x;
+        sc[2 * i + 1] = f.y;
+      }
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[mt][j][0] = fmaf(sc[j], part[mt][j][0], acc[mt][j][0]);
+          acc[mt][j][1] = fmaf(sc[j], part[mt][j][1], acc[mt][j][1]);
+          acc[mt][j][2] = fmaf(sc[4 + j], part[mt][j][2], acc[mt][j][2]);
+          acc[mt][j][3] = fmaf(sc[4 + j], part[mt][j][3], acc[mt][j][3]);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) part[mt][j][r] = 0.f;
+        }
+    };
+
+    int grp_end = -1;
+    for (int li = warp; li < nloc; li += C) {
+      const int slot = li % a.ring;
+      if (!mbar_wait(&full[slot], (li / a.ring) & 1, &abort_flag)) break;
+      const uint32_t base = smem_s + slot * a.stage_bytes;
+      const int k0 = (sb + li) * kBoxRows;
+      const int gbase = k0 / a.G;
+      const int steps = min(kBoxRows, a.K - k0) / 16;  // K is a multiple of 16
+#pragma unroll 2
+      for (int s = 0; s < steps; ++s) {
+        const int k = k0 + 16 * s;
+        if (k >= grp_end || k < grp_end - a.G) {  // a new quantization group (no division per step)
+          if (cur_grp >= 0) flush();
+          const int grp = k / a.G;
+          grp_end = (grp + 1) * a.G;
+          const uint32_t gslot = static_cast<uint32_t>(grp - gbase);
+          zero_consts(lds_u32(base + a.z_off + gslot * (kStripWords * 4) + 4 * g), zc);
+          const uint4 sv = lds_v4(base + a.s_off + gslot * (kStripCols * 2) + 16 * g);
+          sh[0] = sv.x;
+          sh[1] = sv.y;
+          sh[2] = sv.z;
+          sh[3] = sv.w;
+          cur_grp = grp;
+        }
+        const uint32_t wrow = base + s * 16 * (kStripWords * 4);
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) w[q] = lds_u32(wrow + roff[q]);
+        const uint32_t za[4] = {zc[0], zc[1], zc[2], zc[3]};
+        const uint32_t zb[4] = {zc[4], zc[5], zc[6], zc[7]};
+        uint32_t oa[4], ob[4], oc[4], od[4];
+        unpack_pairs(prmt(w[0], w[1], 0x6420u), za, oa);
+        unpack_pairs(prmt(w[0], w[1], 0x7531u), zb, ob);
+        unpack_pairs(prmt(w[2], w[3], 0x6420u), za, oc);
+        unpack_pairs(prmt(w[2], w[3], 0x7531u), zb, od);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          uint32_t b0 = 0u, b1 = 0u;
+          if (xok[mt]) {
+            const uint32_t xa = base + a.x_off + xrow[mt] + s * 32;
+            b0 = lds_u32(xa);
+            b1 = lds_u32(xa + 16);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int sl = ((j & 1) << 1) | (j >> 1);
+            const uint32_t A[4] = {oa[sl], ob[sl], oc[sl], od[sl]};
+            mma_16816(part[mt][j], A, b0, b1);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    if (cur_grp >= 0) flush();
+  }
+
+  // ---------------- sum the C warps' partial tiles ----------------
+  __syncthreads();  // every stage consumed: reuse the ring
+  float* red = reinterpret_cast<float*>(smem);  // [C][MT*8 tokens][64 columns + 4 pad]
+  constexpr int kTok = MT * 8;
+  constexpr int kRow = kStripCols + 4;
+  if (warp < C) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float* r0 = red + (warp * kTok + 8 * mt + 2 * t) * kRow + 8 * g;
+        r0[j] = acc[mt][j][0];
+        r0[kRow + j] = acc[mt][j][1];
+        r0[4 + j] = acc[mt][j][2];
+        r0[kRow + 4 + j] = acc[mt][j][3];
+      }
+  }
+  __syncthreads();
+  const bool failed = abort_flag != 0;
+  // The CTA's partial tile [M][64] goes to row 0.. of the reduction area.
+  float* tile_sum = red + C * kTok * kRow;
+  for (int i = threadIdx.x; i < a.M * kStripCols; i += 32 * (C + 1)) {
+    const int m = i / kStripCols, c = i % kStripCols;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < C; ++w) v += red[(w * kTok + m) * kRow + c];
+    tile_sum[m * kStripCols + c] = v;
+  }
+  if (a.ksplit == 1) {
+    __syncthreads();
+    if (failed) return;
+    for (int i = threadIdx.x; i < a.M * kStripCols; i += 32 * (C + 1)) {
+      const int m = i / kStripCols, c = i % kStripCols;
+      if (col0 + c < a.N) a.y[m * a.y_ld + col0 + c] = __float2half_rn(tile_sum[m * kStripCols + c]);
+    }
+    return;
+  }
+  // K split across the CTAs of a cluster: CTA r sums column slice r of every
+  // CTA's tile through distributed shared memory, in fixed rank order.
+  cluster_sync();
+  if (!failed) {
+    const int S = a.ksplit;
+    const int c_lo = (static_cast<int>(blockIdx.y) * kStripCols) / S;
+    const int c_hi = ((static_cast<int>(blockIdx.y) + 1) * kStripCols) / S;
+    const int width = c_hi - c_lo;
+    for (int i = threadIdx.x; i < a.M * width; i += 32 * (C + 1)) {
+      const int m = i / width, c = c_lo + i % width;
+      float pq[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) pq[q] = q < S ? ld_shared_cluster_f32(map_shared_rank(tile_sum + m * kStripCols + c, q)) : 0.f;
+      const float v = ((pq[0] + pq[1]) + pq[2]) + pq[3];
+      if (col0 + c < a.N) a.y[m * a.y_ld + col0 + c] = __float2half_rn(v);
+    }
+  }
+  cluster_sync();  // keep shared memory alive until every remote read is done
+}
+
+struct StripPlan {
+  int tiles, stages_total, ksplit, ring, gps, stage_bytes, x_off, s_off, z_off, consumers;
+  uint32_t tx;
+  size_t smem;
+};
+
+int align128(int v) { return (v + 127) / 128 * 128; }
+
+bool wide_consumers() {
+  static const bool on = [] {
+    const char* e = std::getenv("ASHQK_STRIP_C16");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+bool half_sm_budget() {
+  static const bool on = [] {
+    const char* e = std::getenv("ASHQK_STRIP_HALF");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
+bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p) {
+  p->tiles = ceil_div(N, kStripCols);
+  p->stages_total = ceil_div(K, kBoxRows);
+  p->gps = (kBoxRows % G == 0) ? kBoxRows / G : kBoxRows / G + 2;
+  if (p->gps > 256) return false;
+  p->x_off = kWeightBytes;
+  p->s_off = p->x_off + align128(M * kXRowBytes);
+  p->z_off = p->s_off + align128(p->gps * kStripCols * 2);
+  p->stage_bytes = p->z_off + align128(p->gps * kStripWords * 4);
+  p->tx = static_cast<uint32_t>(kWeightBytes + M * kXRowBytes + p->gps * kStripCols * 2 + p->gps * kStripWords * 4);
+  // Split K (one cluster of up to 4 CTAs per strip) only while every CTA still
+  // gets an SM of its own; wide layers (more strips than SMs) are not split.
+  p->ksplit = 1;
+  for (int ks = 4; ks >= 2; --ks)
+    if (p->tiles * ks <= sm_count && ks <= p->stages_total) {
+      p->ksplit = ks;
+      break;
+    }
+  // CTAs that share an SM so that every CTA is resident at once.
+  const int per_sm = std::max(1, ceil_div(p->tiles * p->ksplit, sm_count));
+  // Consumer warps per CTA within the SM's register file (one CTA per SM and
+  // M <= 8 affords 16).
+  if (per_sm >= 3 || (M > 8 && per_sm >= 2))
+    p->consumers = 4;
+  else if (per_sm == 1 && M <= 8 && wide_consumers())
+    p->consumers = 16;
+  else
+    p->consumers = 8;
+  // With half_sm, a CTA takes at most half an SM's shared memory so that the
+  // next kernel's CTAs (programmatic dependent launch) can be resident beside it.
+  const size_t cap = half_sm_budget() ? 110 * 1024 : 224 * 1024;
+  const size_t budget = std::min<size_t>(cap, (228 * 1024) / per_sm - 2048) - 1024;
+  int ring = static_cast<int>(budget / p->stage_bytes);
+  ring = std::min(ring, kMaxStages);
+  const int local = ceil_div(p->stages_total, p->ksplit);
+  ring = std::min(ring, std::max(local, 1));
+  if (ring < 2 && local > 1) return false;
+  p->ring = std::max(ring, 1);
+  const size_t red = static_cast<size_t>(p->consumers) * (M > 8 ? 16 : 8) * (kStripCols + 4) * 4 +
+                     static_cast<size_t>(M) * kStripCols * 4;
+  p->smem = 1024 + std::max(static_cast<size_t>(p->ring) * p->stage_bytes, red);
+  return true;
+}
+
+template <int MT, int C>
+int launch_strip(const StripMaps& maps, const StripArgs& args, int tiles, size_t smem, cudaStream_t stream) {
+  const int ks = args.ksplit;
+  static bool configured[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ASHQK_ERR_CUDA;
+  auto kernel = gemv_strip_kernel<MT, C>;
+  if (!configured[dev]) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+      return ASHQK_ERR_CUDA;
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles, ks);
+  cfg.blockDim = dim3(32 * (C + 1));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (ks > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = ks;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  if (cudaLaunchKernelEx(&cfg, kernel, maps, args) != cudaSuccess) return ASHQK_ERR_CUDA;
+  return ASHQK_OK;
+}
+
+}  // namespace
+
+bool gemv_strip_eligible(const void* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
+                         int64_t qz_ld, const void* s, int64_t s_ld, int M, int N, int G) {
+  return M >= 1 && M <= 16 && N % 32 == 0 && G % 16 == 0 && aligned(qw, 16) && qw_ld % 4 == 0 && aligned(qz, 16) &&
+         qz_ld % 4 == 0 && aligned(s, 16) && s_ld % 8 == 0 && aligned(x, 16) && x_ld % 8 == 0;
+}
+
+int gemv_strip_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
+                      int64_t qz_ld, const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K, int G,
+                      int sm_count, cudaStream_t stream) {
+  StripPlan p;
+  if (!plan_strip(M, N, K, G, sm_count, &p)) return ASHQK_ERR_UNSUPPORTED;
+  StripMaps maps;
+  int rc = encode_tensor_map_2d(&maps.qw, CU_TENSOR_MAP_DATA_TYPE_INT32, const_cast<int32_t*>(qw), N / 8, K,
+                                static_cast<uint64_t>(qw_ld) * 4, kStripWords, kBoxRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc)
+    rc = encode_tensor_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<__half*>(x), K, M,
+                              static_cast<uint64_t>(x_ld) * 2, kBoxRows, M, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc)
+    rc = encode_tensor_map_2d(&maps.s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<__half*>(s), N, K / G,
+                              static_cast<uint64_t>(s_ld) * 2, kStripCols, p.gps, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc)
+    rc = encode_tensor_map_2d(&maps.z, CU_TENSOR_MAP_DATA_TYPE_INT32, const_cast<int32_t*>(qz), N / 8, K / G,
+                              static_cast<uint64_t>(qz_ld) * 4, kStripWords, p.gps, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  StripArgs a;
+  a.y = y;
+  a.y_ld = y_ld;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.G = G;
+  a.stages_total = p.stages_total;
+  a.ksplit = p.ksplit;
+  a.ring = p.ring;
+  a.gps = p.gps;
+  a.stage_bytes = p.stage_bytes;
+  a.x_off = p.x_off;
+  a.s_off = p.s_off;
+  a.z_off = p.z_off;
+  a.tx_bytes = p.tx;
+  if (M > 8) {
+    return p.consumers == 4 ? launch_strip<2, 4>(maps, a, p.tiles, p.smem, stream)
+                            : launch_strip<2, 8>(maps, a, p.tiles, p.smem, stream);
+  }
+  if (p.consumers == 16) return launch_strip<1, 16>(maps, a, p.tiles, p.smem, stream);
+  return p.consumers == 4 ? launch_strip<1, 4>(maps, a, p.tiles, p.smem, stream)
+                          : launch_strip<1, 8>(maps, a, p.tiles, p.smem, stream);
+}
+
+}  // namespace ashqk

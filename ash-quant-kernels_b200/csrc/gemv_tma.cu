@@ -388,8 +388,13 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__(MT == 1 ? 112 : 168) gem
       const int width = c_hi - c_lo;
       for (int i = threadIdx.x; i < a.M * width; i += kThreads) {
         const int m = i / width, c = c_lo + i % width;
+        float part_q[kMaxCluster];
+#pragma unroll
+        for (int q = 0; q < kMaxCluster; ++q)
+          part_q[q] = q < S ? ld_shared_cluster_f32(map_shared_rank(red + m * kTileCols + c, q)) : 0.f;
         float v = 0.f;
-        for (int q = 0; q < S; ++q) v += ld_shared_cluster_f32(map_shared_rank(red + m * kTileCols + c, q));
+#pragma unroll
+        for (int q = 0; q < kMaxCluster; ++q) v += part_q[q];  // fixed rank order
         if (c < cols_valid) a.y[m * a.y_ld + col0 + c] = __float2half_rn(v);
       }
     }
@@ -409,9 +414,12 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__(MT == 1 ? 112 : 168) gem
   // ---------------- split-K through workspace slots ----------------
   float* slot = a.ws + (static_cast<int64_t>(tile) * a.splits + split) * a.M * kTileCols;
   for (int m = 0; m < a.M; ++m) slot[m * kTileCols + col] = red[m * kTileCols + col];
-  __threadfence();
   named_barrier_sync(1, kTileCols);
-  if (threadIdx.x == 0) is_last = (atomicAdd(a.counters + tile, 1) == a.splits - 1);
+  // One fence after the barrier publishes the whole CTA's slot (cumulativity).
+  if (threadIdx.x == 0) {
+    __threadfence();
+    is_last = (atomicAdd(a.counters + tile, 1) == a.splits - 1);
+  }
   named_barrier_sync(1, kTileCols);
   if (!is_last) return;
   __threadfence();

@@ -169,9 +169,11 @@ __device__ __forceinline__ uint32_t map_shared_rank(const void* p, uint32_t rank
   return r;
 }
 
+// Not volatile and no memory clobber: callers order these reads with
+// cluster_sync(), so independent remote loads can be in flight together.
 __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  asm("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
   return v;
 }
 

@@ -404,7 +404,7 @@ def run_gpu(args):
         line["roofline"] = {
             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 3), "peak_kind": peak_kind,
-            "traffic": load_traffic(), "kernel": "gemv_kernel<1,true> (decode GEMV, M=1)",
+            "traffic": load_traffic(), "kernel": "gemv_strip_kernel (decode GEMV, M=1; all four layer types)",
             "per_layer": layer_bw,
         }
         value, threads, desc, _ = cpu_reference_sample(1000, 1, budget_s=args.cpu_seconds)

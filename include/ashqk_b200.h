@@ -102,11 +102,11 @@ ASHQK_API int ashqk_w4a16_gemv_noalloc(const void* x, int64_t x_ld, const int32_
 
 /*
  * Selects the decode GEMV kernel for later calls in this process: 0 = automatic
- * (the TMA-pipelined kernel whenever N % 32 == 0 and qweight rows are 16-byte
- * aligned, else the register-streaming kernel), 1 = always the
- * register-streaming kernel, 2 = always the TMA kernel (ineligible problems
- * then return ASHQK_ERR_UNSUPPORTED). No reference counterpart: a test and
- * tuning switch.
+ * (column strips over the whole K when N % 32 == 0, rows are 16-byte aligned
+ * and no split_k is requested; else the split-K TMA kernel when eligible; else
+ * the register-streaming kernel), 1 = always register-streaming, 2 = always
+ * split-K TMA, 3 = always column strips (ineligible problems then return
+ * ASHQK_ERR_UNSUPPORTED). No reference counterpart: a test and tuning switch.
  */
 ASHQK_API int ashqk_set_gemv_kernel(int which);
 
