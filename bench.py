@@ -126,8 +126,8 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(world):
-    return {
+def workload_config(world, n_layers=N_LAYERS):
+    cfg = {
         "workload": "BASELINE config 3: 36-layer Qwen3-8B-shape linear stack (qkv 4096->6144, o 4096->4096, "
                     "gate_up 4096->24576, down 12288->4096), M=1 (M=4 reported too), int4 AWQ G=128, "
                     "CUDA-graph replay",
@@ -136,6 +136,10 @@ def workload_config(world):
         "parallelism": f"tp{world}" if world > 1 else "none",
         "l2": "inputs larger than L2: 3.6 GB of distinct per-layer weights per step",
     }
+    if n_layers != N_LAYERS:  # a reduced stack (profiling runs), not the benchmark workload
+        cfg["decoder_layers"] = n_layers
+        cfg["l2"] = f"{n_layers} layers x 96.5 MB of distinct weights per step"
+    return cfg
 
 
 # ---------------------------------------------------------------------------
@@ -206,7 +210,7 @@ class ClockSampler:
 # GPU arm
 # ---------------------------------------------------------------------------
 
-def make_stack(world, rank, device):
+def make_stack(world, rank, device, n_layers=N_LAYERS):
     """Random AWQ weights for 36 layers; TP-sharded when world > 1.
 
     q, z are uniform over 0..15 (random 32-bit words), scales ~ U(0.002, 0.02),
@@ -216,7 +220,7 @@ def make_stack(world, rank, device):
 
     gen = torch.Generator(device=device)
     stack = []
-    for li in range(N_LAYERS):
+    for li in range(n_layers):
         layer = {}
         for j, (name, n, k) in enumerate(LAYERS):
             gen.manual_seed(1000 * li + j)
@@ -306,6 +310,39 @@ def per_layer_gemv(stack, m, torch, reps=3):
     return res
 
 
+def cublas_fp16_stack(stack, steps, warmup, torch):
+    """us per step of the same stack with fp16 weights through cuBLAS (x @ W), at M=1 and M=4.
+
+    The yardstick the reference compares against: dequantise once (bit-exact
+    kernel), then plain fp16 GEMMs, chained and graph-replayed like the W4A16 stack.
+    """
+    from ashqk import _ext
+
+    deq = [{nm: _ext.ops().dequantize_awq(*layer[nm], torch.float16) for nm, _, _ in LAYERS} for layer in stack]
+    res = {}
+    for m in (1, 4):
+        h = torch.randn(m, 4096, device="cuda").half()
+
+        def step():
+            for w in deq:
+                a = h @ w["qkv"]
+                b = a[:, :4096] @ w["o"]
+                c = b @ w["gate_up"]
+                out = c[:, :12288] @ w["down"]
+            return out
+
+        step()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        res[m] = time_graph(g, max(steps // 2, 10), warmup, torch, None, 1) * 1e3
+        del g
+    del deq
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -325,7 +362,7 @@ def run_gpu(args):
 
     from ashqk import w4a16_linear  # noqa: F401  (loads the extension)
 
-    stack = make_stack(world, rank, device)
+    stack = make_stack(world, rank, device, args.layers)
     hbm_peak, peak_kind = load_peaks()
     results = {}
     graphs = {}
@@ -369,6 +406,7 @@ def run_gpu(args):
 
     d2h_bytes = int(out1.numel()) * out1.element_size()
     layer_bw = per_layer_gemv(stack, 1, torch) if world == 1 else None
+    cublas_us = cublas_fp16_stack(stack, args.steps, warmup, torch) if world == 1 else None
 
     graphs.clear()
     del g1, out1
@@ -380,23 +418,31 @@ def run_gpu(args):
 
     per_rank_bytes = sum(w4a16_bytes(1, n // (world if nm in ("qkv", "gate_up") else 1),
                                      k // (world if nm in ("o", "down") else 1), GROUP)
-                         for nm, n, k in LAYERS) * N_LAYERS
+                         for nm, n, k in LAYERS) * len(stack)
     stack_gbs = per_rank_bytes / (ms1 * 1e-3) / 1e9
     line = {
         "metric": METRIC, "value": round(ms1 * 1e3, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": warmup, "ms_per_step": round(ms1, 4), "higher_is_better": False, "scaling": "strong",
         "vs_baseline": None, "dtype": "fp16 activations x int4 weights, fp32 accumulate", "data": "synthetic",
-        "config": workload_config(world),
+        "config": workload_config(world, len(stack)),
         "m4_us_per_token": round(ms4 * 1e3 / 4, 1), "m4_us_per_step": round(ms4 * 1e3, 1),
         "stack_hbm_gbs_per_gpu": round(stack_gbs, 1),
         "stack_hbm_frac": round(stack_gbs / hbm_peak, 3),
-        "gpu_launches": args.steps * len(LAYERS) * N_LAYERS,
+        "gpu_launches": args.steps * len(LAYERS) * len(stack),
         "clocks": clocks.summary(),
         "e2e": {"value": round(e2e_ms * 1e3, 1), "unit": UNIT, "h2d_bytes_per_step": 4096 * 2,
                 "d2h_bytes_per_step": d2h_bytes,
-                "how": "pinned H2D of the token's hidden state + CUDA-graph replay of the 144 "
-                       "public-API w4a16_linear calls + D2H of the last output, CUDA events"},
+                "how": f"pinned H2D of the token's hidden state + CUDA-graph replay of the "
+                       f"{len(LAYERS) * len(stack)} public-API w4a16_linear calls + D2H of the last output, "
+                       "CUDA events"},
     }
+    if cublas_us is not None:
+        line["cublas_fp16"] = {
+            "us_per_token": round(cublas_us[1], 1), "m4_us_per_step": round(cublas_us[4], 1),
+            "speedup_m1": round(cublas_us[1] / (ms1 * 1e3), 2), "speedup_m4": round(cublas_us[4] / (ms4 * 1e3), 2),
+            "how": "x @ W_fp16 (torch.matmul -> cuBLAS) on the dequantised weights of the same stack, "
+                   "same chaining, CUDA graph, CUDA events",
+        }
     if layer_bw is not None:
         tot_bytes = sum(w4a16_bytes(1, n, k, GROUP) for _, n, k in LAYERS)
         tot_us = sum(layer_bw[nm]["us"] for nm, _, _ in LAYERS)
@@ -404,9 +450,13 @@ def run_gpu(args):
         line["roofline"] = {
             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 3), "peak_kind": peak_kind,
-            "traffic": load_traffic(), "kernel": "gemv_strip_kernel (decode GEMV, M=1; all four layer types)",
+            "traffic": load_traffic(), "algorithmic_bytes": tot_bytes,
+            "per": "one launch of each layer type (qkv, o, gate_up, down) at M=1; achieved = their "
+                   "algorithmic bytes / their summed CUDA-event time",
+            "kernel": "gemv_strip_kernel (decode GEMV, M=1; all four layer types)",
             "per_layer": layer_bw,
         }
+    if layer_bw is not None and args.cpu_seconds > 0:
         value, threads, desc, _ = cpu_reference_sample(1000, 1, budget_s=args.cpu_seconds)
         line["cpu_baseline"] = {"value": round(value, 1), "unit": UNIT, "cores": threads, "kind": "port",
                                 "sample": desc}
@@ -414,11 +464,12 @@ def run_gpu(args):
 
 
 def load_traffic():
-    """DRAM bytes per GEMV launch from the committed ncu summary, if one exists."""
+    """DRAM bytes (read + write) of one launch of each layer type at M=1, summed,
+    from the committed ncu capture summary, if one exists."""
     path = os.path.join(ROOT, "profiles", "gemv_decode_traffic.json")
     try:
         with open(path) as f:
-            return json.load(f).get("bytes_per_launch_stack_avg")
+            return json.load(f).get("dram_bytes_per_layer_set")
     except Exception:
         return None
 
@@ -429,7 +480,10 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU baseline sample")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="budget of the CPU baseline sample (0 skips it)")
+    ap.add_argument("--layers", type=int, default=N_LAYERS,
+                    help="decoder layers in the stack (36 is the benchmark; fewer for profiling runs)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
