@@ -111,6 +111,14 @@ ASHQK_API int ashqk_w4a16_gemv_noalloc(const void* x, int64_t x_ld, const int32_
 ASHQK_API int ashqk_set_gemv_kernel(int which);
 
 /*
+ * Selects the prefill GEMM kernel for later calls in this process: 0 = automatic
+ * (tcgen05 when the problem is eligible, else the chunked GEMV), 1 = always the
+ * chunked GEMV, 2 = always tcgen05 (ineligible problems then return
+ * ASHQK_ERR_UNSUPPORTED). No reference counterpart: a test and tuning switch.
+ */
+ASHQK_API int ashqk_set_gemm_kernel(int which);
+
+/*
  * Reads (and with clear != 0 resets) the device error word of the current
  * device after synchronising it. Bit 1: a pipeline wait inside a kernel ran
  * past its time limit and the kernel gave up (its output and any split-K
@@ -120,15 +128,21 @@ ASHQK_API int ashqk_set_gemv_kernel(int which);
 ASHQK_API int ashqk_get_device_errors(unsigned int* bits, int clear);
 
 /*
- * Bytes of workspace ashqk_w4a16_gemm needs (0 today: the prefill GEMM does not
- * split K). Replaces the sizing of ashqk/kernels/w4a16_gemm_v3.py:108-119.
+ * Bytes of workspace ashqk_w4a16_gemm may need: 0 for the tcgen05 kernel; the
+ * chunked-GEMV fallback (shapes the tcgen05 kernel does not take) needs the
+ * decode GEMV's split-K workspace. Replaces the sizing of
+ * ashqk/kernels/w4a16_gemm_v3.py:108-119.
  */
 ASHQK_API int ashqk_gemm_workspace_size(int M, int N, int K, int group_size, size_t* bytes);
 
 /*
  * Prefill GEMM, any M >= 1: y = x @ deq(...). int4 is dequantised into shared
- * memory and fed to tcgen05.mma with the accumulator in tensor memory.
- * Replaces ashqk/kernels/w4a16_gemm_v3.py:131-171 (w4a16_gemm_v3).
+ * memory and fed to tcgen05.mma with the accumulator in tensor memory, for
+ * N % 128 == 0, K % 64 == 0, group size 16, 32 or a multiple of 64, 16-byte
+ * aligned bases and leading dimensions (x, scales, y in multiples of 8 halves;
+ * qweight, qzeros in multiples of 4 words). Other valid problems run the decode
+ * GEMV over 16-row chunks. Replaces ashqk/kernels/w4a16_gemm_v3.py:131-171
+ * (w4a16_gemm_v3).
  */
 ASHQK_API int ashqk_w4a16_gemm(const void* x, int64_t x_ld, const int32_t* qweight, int64_t qw_ld,
                      const int32_t* qzeros, int64_t qz_ld, const void* scales, int64_t s_ld,
