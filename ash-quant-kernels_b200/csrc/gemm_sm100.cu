@@ -33,7 +33,7 @@ extern "C" int ashqk_w4a16_gemm(const void* x, int64_t x_ld, const int32_t* qwei
   const int impl = ashqk::gemm_impl();
   const bool tc_ok =
       ashqk::gemm_tc_eligible(x, x_ld, qweight, qw_ld, qzeros, qz_ld, scales, s_ld, y, y_ld, N, K, group_size);
-  if (impl == 2 && !tc_ok) return ASHQK_ERR_UNSUPPORTED;
+  if (impl >= 2 && !tc_ok) return ASHQK_ERR_UNSUPPORTED;
   if (tc_ok && impl != 1) {
     ashqk::DeviceInfo info;
     rc = ashqk::device_info(&info);

@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-int g_gemm_impl = 0;  // 0 auto, 1 chunked decode GEMV, 2 tcgen05
+int g_gemm_impl = 0;  // 0 auto, 1 chunked decode GEMV, 2 tcgen05, 3 tcgen05 one CTA, 4 tcgen05 CTA pairs
 
 template <int BN>
 int launch_gemm_tc(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz, int64_t qz_ld,
@@ -392,9 +392,21 @@ bool gemm_tc_eligible(const void* x, int64_t x_ld, const int32_t* qw, int64_t qw
          qz_ld % 4 == 0 && aligned(s, 16) && s_ld % 8 == 0 && aligned(y, 16) && y_ld % 8 == 0;
 }
 
+bool gemm_tc_pair_eligible(int M, int N);
+int gemm_tc_pair_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
+                        int64_t qz_ld, const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K,
+                        int G, int sm_count, cudaStream_t stream);
+
 int gemm_tc_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz, int64_t qz_ld,
                    const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K, int G, int sm_count,
                    cudaStream_t stream) {
+  // CTA pairs (cta_group::2) only when asked for: on B200 they measure slower
+  // than one CTA per tile (their TMA loads see about twice the latency under
+  // load), so the automatic choice is the one-CTA kernel.
+  if (g_gemm_impl == 4) {
+    if (!gemm_tc_pair_eligible(M, N)) return ASHQK_ERR_UNSUPPORTED;
+    return gemm_tc_pair_launch(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G, sm_count, stream);
+  }
   // 256-column tiles unless that leaves most SMs idle and 128 columns divide N.
   const int tiles256 = N % 256 == 0 ? ceil_div(M, kBM) * (N / 256) : 0;
   if (tiles256 > 0 && (tiles256 >= sm_count || N % 128 != 0))
@@ -407,7 +419,7 @@ int gemm_impl() { return g_gemm_impl; }
 }  // namespace ashqk
 
 extern "C" int ashqk_set_gemm_kernel(int which) {
-  if (which < 0 || which > 2) return ASHQK_ERR_INVALID_ARGUMENT;
+  if (which < 0 || which > 4) return ASHQK_ERR_INVALID_ARGUMENT;
   ashqk::g_gemm_impl = which;
   return ASHQK_OK;
 }

@@ -17,6 +17,8 @@
 // Warps: one producer (lane 0 issues all TMA loads) and C consumer warps. Stage
 // i belongs to consumer warp i % C, which runs all 16 of its 16-row steps with
 // no further synchronisation and keeps one quantization group for G/16 steps.
+// When the ring is smaller than the CTA's stage count it holds a multiple of C
+// slots, so each slot serves a single warp (phase parities never alias).
 // A lane unpacks one word (8 columns) of rows {2t, 2t+1, 2t+8, 2t+9} per step
 // -- the k order of an mma.sync A fragment -- with the prmt / LOP3 / HSUB2 code
 // of csrc/awq_unpack.cuh, and mma.sync.m16n8k16 accumulates sum x (q - z) per
@@ -357,7 +359,16 @@ bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p) {
   ring = std::min(ring, kMaxStages);
   const int local = ceil_div(p->stages_total, p->ksplit);
   ring = std::min(ring, std::max(local, 1));
-  if (ring < 2 && local > 1) return false;
+  if (ring < local) {
+    // Slots are reused. A consumer warp tells a slot's fills apart only by
+    // mbarrier phase parity, so it must never wait on a slot whose previous
+    // fill has not landed yet: that happens when another warp's stage sits in
+    // the slot. With ring a multiple of C, slot j only ever holds the stages
+    // of warp j % C, which that warp consumes in order.
+    while (p->consumers > 4 && ring < p->consumers) p->consumers /= 2;
+    ring = ring / p->consumers * p->consumers;
+    if (ring < p->consumers) return false;
+  }
   p->ring = std::max(ring, 1);
   const size_t red = static_cast<size_t>(p->consumers) * (M > 8 ? 16 : 8) * (kStripCols + 4) * 4 +
                      static_cast<size_t>(M) * kStripCols * 4;
@@ -417,6 +428,7 @@ int gemv_strip_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t 
                       int sm_count, cudaStream_t stream) {
   StripPlan p;
   if (!plan_strip(M, N, K, G, sm_count, &p)) return ASHQK_ERR_UNSUPPORTED;
+  if (p.ring < ceil_div(p.stages_total, p.ksplit) && p.ring % p.consumers != 0) return ASHQK_ERR_UNSUPPORTED;
   StripMaps maps;
   int rc = encode_tensor_map_2d(&maps.qw, CU_TENSOR_MAP_DATA_TYPE_INT32, const_cast<int32_t*>(qw), N / 8, K,
                                 static_cast<uint64_t>(qw_ld) * 4, kStripWords, kBoxRows, CU_TENSOR_MAP_SWIZZLE_NONE);

@@ -343,6 +343,110 @@ def cublas_fp16_stack(stack, steps, warmup, torch):
     return res
 
 
+PREFILL_M = (128, 512, 2048, 8192)
+PREFILL_LAYERS = (("gate_up", 24576, 4096), ("down", 4096, 12288))
+TP_MLP = (("gate_up", 57344, 8192), ("down", 8192, 28672))
+TP_M = (1, 16, 4096)
+
+
+def random_awq(n, k, seed, device, torch):
+    """Random AWQ tensors for an [K, N] layer: q, z uniform over 0..15, scales ~ U(0.002, 0.02)."""
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (k, n // 8), dtype=torch.int32, device=device, generator=gen)
+    qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (k // GROUP, n // 8), dtype=torch.int32, device=device, generator=gen)
+    s = (torch.rand((k // GROUP, n), device=device, generator=gen) * 0.018 + 0.002).half()
+    return qw, qz, s
+
+
+def time_flushed(fn, reps, warmup, torch, flush):
+    """Median CUDA-event time (us) of fn() with the L2 flushed (a 256 MB write) before every rep."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) * 1e3)
+    times.sort()
+    return times[len(times) // 2]
+
+
+def prefill_gemm(ms, reps, warmup, torch, tensor_peak):
+    """the prefill GEMM (tcgen05 kernel) on gate_up and down, TFLOP/s = 2MNK / time,
+    beside cuBLAS fp16 on the dequantised weights (x @ W_fp16)."""
+    from ashqk import _ext, w4a16_linear
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    res = {}
+    for j, (name, n, k) in enumerate(PREFILL_LAYERS):
+        qw, qz, s = random_awq(n, k, 77 + j, "cuda", torch)
+        w16 = _ext.ops().dequantize_awq(qw, qz, s, torch.float16)
+        for m in ms:
+            x = torch.randn(m, k, device="cuda").half()
+            us = time_flushed(lambda: w4a16_linear(x, qw, qz, s), reps, warmup, torch, flush)
+            us_cb = time_flushed(lambda: x @ w16, reps, warmup, torch, flush)
+            tf = 2.0 * m * n * k / us / 1e6
+            res[f"{name}_m{m}"] = {"us": round(us, 1), "tflops": round(tf, 1),
+                                   "frac_of_peak": round(tf / tensor_peak, 3),
+                                   "cublas_fp16_us": round(us_cb, 1),
+                                   "cublas_fp16_tflops": round(2.0 * m * n * k / us_cb / 1e6, 1)}
+            del x
+        del qw, qz, s, w16
+    del flush
+    torch.cuda.empty_cache()
+    return res
+
+
+def tp_mlp(world, rank, group, reps, warmup, torch, dist):
+    """a large dense MLP under tensor parallelism (gate_up K=8192 N=57344
+    column-parallel + NCCL all-gather; down K=28672 N=8192 row-parallel + all-reduce), per M:
+    device time of the two layers with their collectives, max over ranks."""
+    from ashqk import tp
+
+    layers = {}
+    for j, (name, n, k) in enumerate(TP_MLP):
+        if name == "gate_up":
+            layers[name] = random_awq(n // world, k, 300 + 10 * rank + j, "cuda", torch)
+        else:
+            layers[name] = random_awq(n, k // world, 300 + 10 * rank + j, "cuda", torch)
+    res = {}
+    for m in TP_M:
+        x = torch.randn(m, TP_MLP[0][2], device="cuda").half()
+        xd = torch.randn(m, TP_MLP[1][2] // world, device="cuda").half()
+
+        def step():
+            tp.column_parallel_linear(x, *layers["gate_up"], group=group)
+            tp.row_parallel_linear(xd, *layers["down"], group=group)
+
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / reps
+        if world > 1:
+            t = torch.tensor([us], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = float(t.item())
+        flops = sum(2.0 * m * n * k for _, n, k in TP_MLP)
+        res[f"m{m}"] = {"us": round(us, 1), "tflops_total": round(flops / us / 1e6, 1)}
+    del layers
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -362,8 +466,14 @@ def run_gpu(args):
 
     from ashqk import w4a16_linear  # noqa: F401  (loads the extension)
 
-    stack = make_stack(world, rank, device, args.layers)
     hbm_peak, peak_kind = load_peaks()
+    tensor_peak, tensor_kind = load_tensor_peak()
+    if args.only == "prefill":  # profiling runs of the prefill GEMM alone
+        res = prefill_gemm(args.prefill_m or PREFILL_M, args.steps, warmup, torch, tensor_peak)
+        if rank == 0:
+            print(json.dumps({"prefill": res}), flush=True)
+        return
+    stack = make_stack(world, rank, device, args.layers)
     results = {}
     graphs = {}
     for m in (1, 4):
@@ -407,6 +517,11 @@ def run_gpu(args):
     d2h_bytes = int(out1.numel()) * out1.element_size()
     layer_bw = per_layer_gemv(stack, 1, torch) if world == 1 else None
     cublas_us = cublas_fp16_stack(stack, args.steps, warmup, torch) if world == 1 else None
+    n_layers = len(stack)
+    del stack
+    torch.cuda.empty_cache()
+    prefill = prefill_gemm(PREFILL_M, 10, warmup, torch, tensor_peak) if world == 1 and args.only == "all" else None
+    tp_res = tp_mlp(world, rank, group, 10, warmup, torch, dist) if args.only == "all" else None
 
     graphs.clear()
     del g1, out1
@@ -418,22 +533,22 @@ def run_gpu(args):
 
     per_rank_bytes = sum(w4a16_bytes(1, n // (world if nm in ("qkv", "gate_up") else 1),
                                      k // (world if nm in ("o", "down") else 1), GROUP)
-                         for nm, n, k in LAYERS) * len(stack)
+                         for nm, n, k in LAYERS) * n_layers
     stack_gbs = per_rank_bytes / (ms1 * 1e-3) / 1e9
     line = {
         "metric": METRIC, "value": round(ms1 * 1e3, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": warmup, "ms_per_step": round(ms1, 4), "higher_is_better": False, "scaling": "strong",
         "vs_baseline": None, "dtype": "fp16 activations x int4 weights, fp32 accumulate", "data": "synthetic",
-        "config": workload_config(world, len(stack)),
+        "config": workload_config(world, n_layers),
         "m4_us_per_token": round(ms4 * 1e3 / 4, 1), "m4_us_per_step": round(ms4 * 1e3, 1),
         "stack_hbm_gbs_per_gpu": round(stack_gbs, 1),
         "stack_hbm_frac": round(stack_gbs / hbm_peak, 3),
-        "gpu_launches": args.steps * len(LAYERS) * len(stack),
+        "gpu_launches": args.steps * len(LAYERS) * n_layers,
         "clocks": clocks.summary(),
         "e2e": {"value": round(e2e_ms * 1e3, 1), "unit": UNIT, "h2d_bytes_per_step": 4096 * 2,
                 "d2h_bytes_per_step": d2h_bytes,
                 "how": f"pinned H2D of the token's hidden state + CUDA-graph replay of the "
-                       f"{len(LAYERS) * len(stack)} public-API w4a16_linear calls + D2H of the last output, "
+                       f"{len(LAYERS) * n_layers} public-API w4a16_linear calls + D2H of the last output, "
                        "CUDA events"},
     }
     if cublas_us is not None:
@@ -442,6 +557,16 @@ def run_gpu(args):
             "speedup_m1": round(cublas_us[1] / (ms1 * 1e3), 2), "speedup_m4": round(cublas_us[4] / (ms4 * 1e3), 2),
             "how": "x @ W_fp16 (torch.matmul -> cuBLAS) on the dequantised weights of the same stack, "
                    "same chaining, CUDA graph, CUDA events",
+        }
+    if prefill is not None:
+        line["prefill_gemm"] = {
+            "kernel": "gemm_tc_kernel (tcgen05.mma, TMEM accumulators)", "peak_tflops": tensor_peak,
+            "peak_kind": tensor_kind, "l2": "flushed (256 MB write) before every timed call", "shapes": prefill,
+        }
+    if tp_res is not None:
+        line["tp_mlp"] = {
+            "config": "gate_up K=8192 N=57344 column-parallel + all-gather, down K=28672 N=8192 row-parallel + "
+                      f"all-reduce, G=128, tp{world}, max over ranks", "per_m": tp_res,
         }
     if layer_bw is not None:
         tot_bytes = sum(w4a16_bytes(1, n, k, GROUP) for _, n, k in LAYERS)
@@ -463,6 +588,15 @@ def run_gpu(args):
     print(json.dumps(line), flush=True)
 
 
+def load_tensor_peak():
+    """Dense fp16/bf16 tensor peak (TFLOP/s): the measured burst cuBLAS figure, else the fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 def load_traffic():
     """DRAM bytes (read + write) of one launch of each layer type at M=1, summed,
     from the committed ncu capture summary, if one exists."""
@@ -482,6 +616,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="budget of the CPU baseline sample (0 skips it)")
+    ap.add_argument("--only", choices=["all", "decode", "prefill"], default="all",
+                    help="decode: the decode stack alone; prefill: only the prefill GEMM (profiling runs)")
+    ap.add_argument("--prefill-m", type=int, nargs="*", default=None, help="M values for --only prefill")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="decoder layers in the stack (36 is the benchmark; fewer for profiling runs)")
     args = ap.parse_args()

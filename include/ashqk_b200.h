@@ -112,9 +112,12 @@ ASHQK_API int ashqk_set_gemv_kernel(int which);
 
 /*
  * Selects the prefill GEMM kernel for later calls in this process: 0 = automatic
- * (tcgen05 when the problem is eligible, else the chunked GEMV), 1 = always the
- * chunked GEMV, 2 = always tcgen05 (ineligible problems then return
- * ASHQK_ERR_UNSUPPORTED). No reference counterpart: a test and tuning switch.
+ * (tcgen05 with one CTA per output tile when the problem is eligible, otherwise
+ * the chunked GEMV), 1 = always the chunked GEMV, 2 = always tcgen05 (one CTA
+ * per tile), 3 = the same, 4 = tcgen05 on CTA pairs (cta_group::2, M = 256 per
+ * instruction; needs M > 128 and N % 256 == 0). Forced choices return
+ * ASHQK_ERR_UNSUPPORTED for problems they do not take. No reference
+ * counterpart: a test and tuning switch.
  */
 ASHQK_API int ashqk_set_gemm_kernel(int which);
 

@@ -33,12 +33,18 @@ def _lib():
     return lib
 
 
-@pytest.fixture(params=[2, 1], ids=["tcgen05", "chunked-gemv"])
+@pytest.fixture(params=[3, 4, 1], ids=["tcgen05-1cta", "tcgen05-pair", "chunked-gemv"])
 def gemm_kernel(request):
+    """Run a test once per prefill GEMM kernel (ashqk_set_gemm_kernel), then restore auto."""
     lib = _lib()
     assert lib.ashqk_set_gemm_kernel(request.param) == 0
     yield request.param
     assert lib.ashqk_set_gemm_kernel(0) == 0
+
+
+def _skip_unless_eligible(impl, m, n):
+    if impl == 4 and not (m > 128 and n % 256 == 0):
+        pytest.skip("the CTA-pair kernel takes M > 128 and N % 256 == 0")
 
 
 def _gemm(x, qw, qz, s):
@@ -60,6 +66,7 @@ def _check(x, qw, qz, s, y, y_true=None):
 @pytest.mark.parametrize("n", [256, 384])
 def test_dequant_tile_bit_exact(n, g, gemm_kernel):
     k = 256
+    _skip_unless_eligible(gemm_kernel, k, n)
     _, qw, qz, s = quantized_problem(1, n, k, g, seed=n + g)
     x = np.eye(k, dtype=np.float16)
     y = _gemm(*to_cuda(x, qw, qz, s))
@@ -78,6 +85,7 @@ def test_dequant_tile_bit_exact(n, g, gemm_kernel):
     (512, 2048, 1024, 128),
 ])
 def test_gemm_parity(m, n, k, g, gemm_kernel):
+    _skip_unless_eligible(gemm_kernel, m, n)
     x, qw, qz, s = quantized_problem(m, n, k, g, seed=m + n + k + g)
     y = _gemm(*to_cuda(x, qw, qz, s))
     torch.cuda.synchronize()
@@ -128,26 +136,38 @@ def test_prefill_configs(layer, m):
 
 def test_kernels_agree():
     lib = _lib()
-    m, n, k, g = 96, 2048, 2048, 128
+    m, n, k, g = 320, 2048, 2048, 128
     x, qw, qz, s = quantized_problem(m, n, k, g, seed=5)
     args = to_cuda(x, qw, qz, s)
     out = {}
-    for impl in (1, 2):
+    for impl in (1, 3, 4):
         assert lib.ashqk_set_gemm_kernel(impl) == 0
         out[impl] = _gemm(*args).float()
     assert lib.ashqk_set_gemm_kernel(0) == 0
-    diff = float((out[1] - out[2]).norm() / out[1].norm())
-    assert diff < 2e-3, diff  # different fp32 summation orders, same fp16 rounding
+    for impl in (3, 4):
+        diff = float((out[1] - out[impl]).norm() / out[1].norm())
+        assert diff < 2e-3, (impl, diff)  # different fp32 summation orders, same fp16 rounding
+    # the one-CTA and pair kernels run the same MMA sequence per output element
+    assert float((out[3] - out[4]).norm() / out[3].norm()) < 2e-3
 
 
 def test_unsupported_shape_when_forced():
     """Forcing tcgen05 on a shape it does not take is an error, not a silent fallback."""
     lib = _lib()
     x, qw, qz, s = quantized_problem(40, 1000, 512, 64, seed=6)
-    assert lib.ashqk_set_gemm_kernel(2) == 0
+    for impl in (2, 3, 4):
+        assert lib.ashqk_set_gemm_kernel(impl) == 0
+        try:
+            with pytest.raises(RuntimeError):
+                _gemm(*to_cuda(x, qw, qz, s))
+        finally:
+            assert lib.ashqk_set_gemm_kernel(0) == 0
+    # the pair kernel also refuses M <= 128 when forced
+    x2, qw2, qz2, s2 = quantized_problem(64, 512, 512, 64, seed=7)
+    assert lib.ashqk_set_gemm_kernel(4) == 0
     try:
         with pytest.raises(RuntimeError):
-            _gemm(*to_cuda(x, qw, qz, s))
+            _gemm(*to_cuda(x2, qw2, qz2, s2))
     finally:
         assert lib.ashqk_set_gemm_kernel(0) == 0
     y = _gemm(*to_cuda(x, qw, qz, s))  # auto: the chunked GEMV takes it

@@ -112,3 +112,39 @@ def test_nccl_tensor_parallel_mlp():
 
     world = min(torch.cuda.device_count(), 8)
     mp.start_processes(_nccl_worker, args=(world, _free_port()), nprocs=world, start_method="spawn", join=True)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+@pytest.mark.parametrize("m", [1, 16, 4096])
+@pytest.mark.parametrize("layer", [("gate_up", 57344, 8192, "column"), ("down", 8192, 28672, "row")])
+def test_tp_mlp_rank_shapes(layer, m, world):
+    """Every rank's layer of the benchmark's tensor-parallel MLP (config 5) on one GPU, at full size.
+
+    One rank's shard is an ordinary layer of N/P columns (column-parallel) or
+    K/P rows (row-parallel); world 1 is the unsharded layer. Truth: fp32 GEMM
+    on the GPU over the bit-exact dequantised weights.
+    """
+    if m == 4096 and world in (2, 4):
+        pytest.skip("prefill shards are covered at P = 1 and 8")
+    from ashqk import _ext, w4a16_linear
+
+    _, n, k, mode = layer
+    n_loc, k_loc = (n // world, k) if mode == "column" else (n, k // world)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(world * 31 + m)
+    qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (k_loc, n_loc // 8), dtype=torch.int32, device="cuda", generator=gen)
+    qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (k_loc // 128, n_loc // 8), dtype=torch.int32, device="cuda",
+                       generator=gen)
+    s = (torch.rand((k_loc // 128, n_loc), device="cuda", generator=gen) * 0.018 + 0.002).half()
+    x = torch.randn(m, k_loc, device="cuda", generator=gen).half()
+    y = w4a16_linear(x, qw, qz, s)
+    w32 = _ext.ops().dequantize_awq(qw, qz, s, torch.float32)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        y_true = x.float() @ w32
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    e_cublas = float(((x @ w32.half()).float() - y_true).norm() / y_true.norm())
+    e = float((y.float() - y_true).norm() / y_true.norm())
+    assert e <= 2 * e_cublas + 1e-5, (e, e_cublas)
