@@ -56,6 +56,42 @@ __device__ __forceinline__ void unpack_raw(uint32_t T, uint32_t (&o)[4]) {
   o[3] = lop3_and_or(T8, kHiNibbles, kMagic1024x2);
 }
 
+// ---- dequantisation of one packed word into 8 fp16 weights (GEMM operand tiles) ----
+//
+// Word w holds columns (0,2,4,6,1,3,5,7) in nibbles 0..7, so masking nibbles
+// {0,4}, {1,5} of w and of w >> 8 yields the column pairs (0,1), (2,3), (4,5),
+// (6,7) as half2 -- a row of 8 consecutive columns. Low nibbles give 1024 + q,
+// from which 1024 + z is subtracted; high nibbles give 1024 + 16 q, scaled by
+// 1/16 and offset by -(64 + z) in one fma. Both give q - z exactly; the product
+// with the fp16 scale is then rounded once, which is the fp32 (q - z) * s of
+// ashqk/ref.py:78-86 rounded to fp16, bit for bit.
+
+// Zero-point constants of one packed qzeros word, for dequant_word.
+__device__ __forceinline__ void word_zero_consts(uint32_t zw, uint32_t (&zc)[4]) {
+  const uint32_t z8 = zw >> 8;
+  zc[0] = lop3_and_or(zw, kLoNibbles, kMagic1024x2);
+  zc[1] = h2_as_u32(__hmul2(u32_as_h2(lop3_and_or(zw, kHiNibbles, kMagic1024x2)), u32_as_h2(kNegSixteenthX2)));
+  zc[2] = lop3_and_or(z8, kLoNibbles, kMagic1024x2);
+  zc[3] = h2_as_u32(__hmul2(u32_as_h2(lop3_and_or(z8, kHiNibbles, kMagic1024x2)), u32_as_h2(kNegSixteenthX2)));
+}
+
+// 8 fp16 weights (q - z) * s of columns 0..7 of packed word w, as 4 half2.
+// sc: the 8 columns' scales as 4 half2 (one 16-byte load of the scale row).
+__device__ __forceinline__ void dequant_word(uint32_t w, const uint32_t (&zc)[4], const uint32_t (&sc)[4],
+                                             uint32_t (&h)[4]) {
+  const uint32_t w8 = w >> 8;
+  const __half2 d0 = __hsub2(u32_as_h2(lop3_and_or(w, kLoNibbles, kMagic1024x2)), u32_as_h2(zc[0]));
+  const __half2 d1 = __hfma2(u32_as_h2(lop3_and_or(w, kHiNibbles, kMagic1024x2)), u32_as_h2(kSixteenthX2),
+                             u32_as_h2(zc[1]));
+  const __half2 d2 = __hsub2(u32_as_h2(lop3_and_or(w8, kLoNibbles, kMagic1024x2)), u32_as_h2(zc[2]));
+  const __half2 d3 = __hfma2(u32_as_h2(lop3_and_or(w8, kHiNibbles, kMagic1024x2)), u32_as_h2(kSixteenthX2),
+                             u32_as_h2(zc[3]));
+  h[0] = h2_as_u32(__hmul2(d0, u32_as_h2(sc[0])));
+  h[1] = h2_as_u32(__hmul2(d1, u32_as_h2(sc[1])));
+  h[2] = h2_as_u32(__hmul2(d2, u32_as_h2(sc[2])));
+  h[3] = h2_as_u32(__hmul2(d3, u32_as_h2(sc[3])));
+}
+
 // Slot of column j (0..7 of a word) in the unpack_pairs output of T_a / T_b.
 __device__ __forceinline__ constexpr int col_slot(int j) { return 4 * (j >> 2) + (((j & 1) << 1) | ((j >> 1) & 1)); }
 

@@ -9,11 +9,11 @@
 //   warp 0        TMA producer: x tile [128 x 64] (128-byte swizzle, the K-major
 //                 A operand as the MMA reads it), packed weights [64 x BN/8] words,
 //                 the scale and zero rows of the stage's groups.
-//   warps 6..13   dequantisers: int4 -> fp16 with W = (q - z) * s computed as
-//                 hsub2 + hmul2 (bit-exact with ashqk/ref.py:78-86, the fp32
-//                 product being exact), written as the MN-major B operand in the
-//                 128-byte-swizzled canonical layout (8 k-rows x 64 columns per
-//                 1 KB atom).
+//   warps 6..21   dequantisers, 4 k rows of each stage per warp: int4 -> fp16,
+//                 W = (q - z) * s with an exact q - z and one rounding of the
+//                 product (bit-exact with ashqk/ref.py:78-86, awq_unpack.cuh),
+//                 written as the MN-major B operand in the 128-byte-swizzled
+//                 canonical layout (8 k-rows x 64 columns per 1 KB atom).
 //   warp 1        one thread issues tcgen05.mma (M=128, N=BN, K=16) x 4 per stage
 //                 into one of two TMEM accumulators, and commits stage releases
 //                 and tile completion to mbarriers.
@@ -25,7 +25,7 @@
 // device error, all roles stop, and TMEM is released before the kernel exits.
 #include <algorithm>
 
-#include "common.cuh"
+#include "awq_unpack.cuh"
 #include "sm100.cuh"
 
 namespace ashqk {
@@ -35,7 +35,7 @@ constexpr int kBM = 128;   // tokens per tile = MMA M = TMEM lanes
 constexpr int kBK = 64;    // K per stage: one 128-byte swizzle row of x
 constexpr int kStagesA = 5;
 constexpr int kStagesB = 2;
-constexpr int kDeqWarps = 8;
+constexpr int kDeqWarps = 16;  // each owns 64 / 16 = 4 k rows of every stage
 constexpr int kEpiWarps = 4;
 constexpr int kFirstEpiWarp = 2;
 constexpr int kFirstDeqWarp = kFirstEpiWarp + kEpiWarps;
@@ -251,13 +251,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- dequantisers ----------------
-    constexpr int WC = L::kWC;
-    constexpr int kRowStep = 32 / WC;           // lanes per row set: 32 (BN 256) or 16 (BN 128)
-    constexpr int kRowsPerThread = 8 / kRowStep;
-    const int d = warp - kFirstDeqWarp;         // this warp owns k rows 8d .. 8d+7 of every stage
-    const int c = lane % WC;                    // packed word column (8 weight columns)
-    const int r0 = 8 * d + lane / WC;
-    const int grp_row = a.G >= kBK ? 0 : (8 * d) / a.G;
+    constexpr int WC = L::kWC;                      // packed words per row of this CTA's columns
+    constexpr int kRowsPerWarp = kBK / kDeqWarps;     // k rows of a stage per warp
+    constexpr int kRowStep = 32 / WC;                 // rows covered by one pass of the warp's lanes
+    constexpr int kRowsPerThread = kRowsPerWarp / kRowStep;
+    static_assert(kRowsPerThread >= 1 && kRowsPerWarp % kRowStep == 0, "dequantiser tiling");
+    const int d = warp - kFirstDeqWarp;               // rows kRowsPerWarp*d .. of every stage
+    const int c = lane % WC;                          // packed word column (8 weight columns)
+    const int r0 = kRowsPerWarp * d + lane / WC;
+    const int grp_row = a.G >= kBK ? 0 : (kRowsPerWarp * d) / a.G;  // group >= 16 >= kRowsPerWarp
     int sa = 0, sb = 0;
     uint32_t pa = 0, pb = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
@@ -275,8 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint4 sv = lds_v4(sa_addr);
         const uint32_t sc[4] = {sv.x, sv.y, sv.z, sv.w};
         uint32_t zc[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) zc[j] = lop3_and_or(zw >> (4 * j), kLoNibbles, kMagic1024x2);
+        word_zero_consts(zw, zc);
         uint32_t wv[kRowsPerThread];
 #pragma unroll
         for (int i = 0; i < kRowsPerThread; ++i) wv[i] = lds_u32(qa + (r0 + i * kRowStep) * (WC * 4) + c * 4);
@@ -284,13 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < kRowsPerThread; ++i) {
           const int kr = r0 + i * kRowStep;
           uint32_t h[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            // nibbles j and j+4 hold columns 2j and 2j+1 (AWQ order 0,2,4,6,1,3,5,7)
-            const __half2 qz = __hsub2(u32_as_h2(lop3_and_or(wv[i] >> (4 * j), kLoNibbles, kMagic1024x2)),
-                                       u32_as_h2(zc[j]));
-            h[j] = h2_as_u32(__hmul2(qz, u32_as_h2(sc[j])));
-          }
+          dequant_word(wv[i], zc, sc, h);
           const uint32_t addr =
               ba + (kr >> 3) * L::kSbo + (kr & 7) * 128u + ((static_cast<uint32_t>(c & 7) ^ (kr & 7)) << 4);
           sts_v4(addr, h[0], h[1], h[2], h[3]);
@@ -400,13 +395,13 @@ int gemm_tc_pair_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_
 int gemm_tc_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz, int64_t qz_ld,
                    const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K, int G, int sm_count,
                    cudaStream_t stream) {
-  // CTA pairs (cta_group::2) only when asked for: on B200 they measure slower
-  // than one CTA per tile (their TMA loads see about twice the latency under
-  // load), so the automatic choice is the one-CTA kernel.
-  if (g_gemm_impl == 4) {
-    if (!gemm_tc_pair_eligible(M, N)) return ASHQK_ERR_UNSUPPORTED;
+  // CTA pairs (cta_group::2) once M spans two 128-row tiles and N % 256 == 0:
+  // each SM then writes and feeds the tensor core half as much of the fp16
+  // weight tile, which bounds the one-CTA kernel (shared-memory bandwidth).
+  const bool pair_ok = gemm_tc_pair_eligible(M, N);
+  if (g_gemm_impl == 4 && !pair_ok) return ASHQK_ERR_UNSUPPORTED;
+  if (pair_ok && g_gemm_impl != 3)
     return gemm_tc_pair_launch(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G, sm_count, stream);
-  }
   // 256-column tiles unless that leaves most SMs idle and 128 columns divide N.
   const int tiles256 = N % 256 == 0 ? ceil_div(M, kBM) * (N / 256) : 0;
   if (tiles256 > 0 && (tiles256 >= sm_count || N % 128 != 0))

@@ -10,8 +10,8 @@
 //
 //   both CTAs   warp 0: TMA of its x rows, packed weights, scales, zeros (plain
 //               loads into its own shared memory, completing on its own barrier);
-//               warps 6..13: dequantise its 128 columns, then arrive on the even
-//               CTA's "B ready" barrier (cluster-scope release);
+//               warps 6..21: dequantise its 128 columns, fence the stores to the
+//               async proxy, then arrive on the even CTA's "B ready" barrier;
 //               warps 2..5: epilogue of its 128 rows from its own TMEM.
 //   even CTA    warp 1, one thread: the pair MMAs, commits multicast to both
 //               CTAs' "stage free" and "accumulator full" barriers.
@@ -20,7 +20,7 @@
 // before releasing it, after every MMA has completed. All waits are bounded.
 #include <algorithm>
 
-#include "common.cuh"
+#include "awq_unpack.cuh"
 #include "sm100.cuh"
 
 namespace ashqk {
@@ -32,7 +32,7 @@ constexpr int kHalfN = 128;  // columns staged per CTA
 constexpr int kBK = 64;
 constexpr int kStagesA = 6;
 constexpr int kStagesB = 3;
-constexpr int kDeqWarps = 8;
+constexpr int kDeqWarps = 16;  // each owns 64 / 16 = 4 k rows of every stage
 constexpr int kEpiWarps = 4;
 constexpr int kFirstEpiWarp = 2;
 constexpr int kFirstDeqWarp = kFirstEpiWarp + kEpiWarps;
@@ -244,14 +244,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (acc == 0) pacc ^= 1u;
     }
   } else {
-    // ---------------- dequantisers (both CTAs) ----------------
-    constexpr int WC = L::kWC;          // 16 packed words per row of this CTA's columns
-    constexpr int kRowStep = 32 / WC;   // 2: lanes 0-15 and 16-31 take alternate rows
-    constexpr int kRowsPerThread = 8 / kRowStep;
-    const int d = warp - kFirstDeqWarp;
-    const int c = lane % WC;
-    const int r0 = 8 * d + lane / WC;
-    const int grp_row = a.G >= kBK ? 0 : (8 * d) / a.G;
+    // ---------------- dequantisers ----------------
+    constexpr int WC = L::kWC;                      // packed words per row of this CTA's columns
+    constexpr int kRowsPerWarp = kBK / kDeqWarps;     // k rows of a stage per warp
+    constexpr int kRowStep = 32 / WC;                 // rows covered by one pass of the warp's lanes
+    constexpr int kRowsPerThread = kRowsPerWarp / kRowStep;
+    static_assert(kRowsPerThread >= 1 && kRowsPerWarp % kRowStep == 0, "dequantiser tiling");
+    const int d = warp - kFirstDeqWarp;               // rows kRowsPerWarp*d .. of every stage
+    const int c = lane % WC;                          // packed word column (8 weight columns)
+    const int r0 = kRowsPerWarp * d + lane / WC;
+    const int grp_row = a.G >= kBK ? 0 : (kRowsPerWarp * d) / a.G;  // group >= 16 >= kRowsPerWarp
     const uint32_t full_b_lead = map_shared_rank(full_b, 0);
     int sa = 0, sb = 0;
     uint32_t pa = 0, pb = 0;
@@ -270,8 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint4 sv = lds_v4(s_addr);
         const uint32_t sc[4] = {sv.x, sv.y, sv.z, sv.w};
         uint32_t zc[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) zc[j] = lop3_and_or(zw >> (4 * j), kLoNibbles, kMagic1024x2);
+        word_zero_consts(zw, zc);
         uint32_t wv[kRowsPerThread];
 #pragma unroll
         for (int i = 0; i < kRowsPerThread; ++i) wv[i] = lds_u32(qa + (r0 + i * kRowStep) * (WC * 4) + c * 4);
@@ -279,12 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < kRowsPerThread; ++i) {
           const int kr = r0 + i * kRowStep;
           uint32_t h[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const __half2 qz = __hsub2(u32_as_h2(lop3_and_or(wv[i] >> (4 * j), kLoNibbles, kMagic1024x2)),
-                                       u32_as_h2(zc[j]));
-            h[j] = h2_as_u32(__hmul2(qz, u32_as_h2(sc[j])));
-          }
+          dequant_word(wv[i], zc, sc, h);
           const uint32_t addr =
               ba + (kr >> 3) * L::kSbo + (kr & 7) * 128u + ((static_cast<uint32_t>(c & 7) ^ (kr & 7)) << 4);
           sts_v4(addr, h[0], h[1], h[2], h[3]);

@@ -112,9 +112,13 @@ __device__ __forceinline__ bool mbar_try_wait_cluster_sleep(uint64_t* bar, uint3
 }
 
 // Arrive on an mbarrier of any CTA in the cluster (address from mapa), with
-// release semantics at cluster scope.
+// the default (CTA-scope release) semantics. Used to hand shared-memory tiles
+// to the pair's MMA-issuing CTA: the writers fence their generic-proxy stores
+// to the async proxy first, which is what the tensor core's reads need. The
+// cluster-scope release form also works but stalls each arriving warp for
+// about a microsecond on B200.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // Bounded wait for the phase with the given parity. Returns false (and flags

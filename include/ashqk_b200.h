@@ -112,12 +112,13 @@ ASHQK_API int ashqk_set_gemv_kernel(int which);
 
 /*
  * Selects the prefill GEMM kernel for later calls in this process: 0 = automatic
- * (tcgen05 with one CTA per output tile when the problem is eligible, otherwise
- * the chunked GEMV), 1 = always the chunked GEMV, 2 = always tcgen05 (one CTA
- * per tile), 3 = the same, 4 = tcgen05 on CTA pairs (cta_group::2, M = 256 per
- * instruction; needs M > 128 and N % 256 == 0). Forced choices return
- * ASHQK_ERR_UNSUPPORTED for problems they do not take. No reference
- * counterpart: a test and tuning switch.
+ * (tcgen05 when the problem is eligible -- on CTA pairs, cta_group::2 with
+ * M = 256 per instruction, when M > 128 and N % 256 == 0, else one CTA per
+ * output tile -- otherwise the chunked GEMV), 1 = always the chunked GEMV,
+ * 2 = always tcgen05 (automatic variant), 3 = tcgen05 on one CTA per tile,
+ * 4 = tcgen05 on CTA pairs. Forced choices return ASHQK_ERR_UNSUPPORTED for
+ * problems they do not take. No reference counterpart: a test and tuning
+ * switch.
  */
 ASHQK_API int ashqk_set_gemm_kernel(int which);
 
