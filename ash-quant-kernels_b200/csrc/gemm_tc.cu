@@ -51,6 +51,7 @@ struct GemmArgs {
   int64_t y_ld;
   int M, N, K, G;
   int tiles_m, tiles_n, num_kb, gps;
+  int ksplit;  // > 1: a cluster of ksplit CTAs shares one tile's K range (one tile per cluster)
 };
 
 template <int BN>
@@ -137,6 +138,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_launch_dependents();
 
   const int tiles = a.tiles_m * a.tiles_n;
+  // With a K split, cluster (blockIdx.x / ksplit) owns one tile and its CTA of
+  // rank `split` the k blocks [kb0, kb1); otherwise CTAs stride over tiles.
+  const int ks = a.ksplit;
+  const int split = ks > 1 ? static_cast<int>(cluster_rank()) : 0;
+  const int t_first = ks > 1 ? static_cast<int>(blockIdx.x) / ks : static_cast<int>(blockIdx.x);
+  const int t_step = ks > 1 ? tiles : static_cast<int>(gridDim.x);
+  const int kb0 = split * a.num_kb / ks, kb1 = (split + 1) * a.num_kb / ks;
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
@@ -144,9 +152,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      for (int t = t_first; t < tiles; t += t_step) {
         const int mb = t % a.tiles_m, nb = t / a.tiles_m;
-        for (int kb = 0; kb < a.num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_a[stage], phase ^ 1u, abort, true)) break;
           mbar_arrive_expect_tx(&full_a[stage], tx);
           const int k0 = kb * kBK;
@@ -176,12 +184,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = umma_idesc_f16_f32(kBM, BN, false, true);
       int sa = 0, sb = 0, acc = 0;
       uint32_t pa = 0, pb = 0, pacc = 0;
-      for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
+      for (int t = t_first; t < tiles && !*abort; t += t_step) {
         if (!mbar_wait(&acc_empty[acc], pacc ^ 1u, abort)) break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         bool ok = true;
-        for (int kb = 0; kb < a.num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_a[sa], pa, abort, true) || !mbar_wait(&full_b[sb], pb, abort, true)) {
             ok = false;
             break;
@@ -194,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // A: K-major, advance 16 halves (32 B) inside the swizzle row.
             // B: MN-major, advance two 8-row k groups.
             umma_f16_ss(d_tmem, umma_desc_sw128(xa + 32u * j, 16u, 1024u),
-                        umma_desc_sw128(ba + 2u * L::kSbo * j, 1024u, L::kSbo), idesc, (kb | j) != 0);
+                        umma_desc_sw128(ba + 2u * L::kSbo * j, 1024u, L::kSbo), idesc, (kb != kb0) || (j != 0));
           }
           umma_commit(&empty_a[sa]);
           umma_commit(&empty_b[sb]);
@@ -221,19 +229,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;  // the TMEM lane quadrant this warp may read
     int acc = 0;
     uint32_t pacc = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    for (int t = t_first; t < tiles; t += t_step) {
       const int mb = t % a.tiles_m, nb = t / a.tiles_m;
       if (!mbar_wait(&acc_full[acc], pacc, abort)) break;
       tc_fence_after_sync();
       const int row = mb * kBM + 32 * quad + lane;
       __half* yrow = a.y + static_cast<int64_t>(row) * a.y_ld + nb * BN;
+      // K split: this CTA's fp32 partial goes to its own shared memory (over the
+      // drained ring), row stride BN + 4 floats; the cluster sums it below.
+      float* prow = reinterpret_cast<float*>(smem) + (32 * quad + lane) * (BN + 4);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(32 * quad) << 16) + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(taddr + c, r);
         tmem_wait_ld();
-        if (row < a.M) {
+        if (ks > 1) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<float4*>(prow + c + 4 * i) = make_float4(
+                __uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]), __uint_as_float(r[4 * i + 2]),
+                __uint_as_float(r[4 * i + 3]));
+        } else if (row < a.M) {
           uint32_t h[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
@@ -262,9 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int grp_row = a.G >= kBK ? 0 : (kRowsPerWarp * d) / a.G;  // group >= 16 >= kRowsPerWarp
     int sa = 0, sb = 0;
     uint32_t pa = 0, pb = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    for (int t = t_first; t < tiles; t += t_step) {
       bool ok = true;
-      for (int kb = 0; kb < a.num_kb; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&full_a[sa], pa, abort) || !mbar_wait(&empty_b[sb], pb ^ 1u, abort)) {
           ok = false;
           break;
@@ -309,6 +326,36 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Teardown: every role has finished (or given up); release TMEM.
   tc_fence_before_sync();
   __syncthreads();
+  if (ks > 1) {
+    // Sum the cluster's partial tiles: CTA `split` owns rows [r0, r1) of the
+    // tile and adds the ranks' partials in fixed order (deterministic).
+    cluster_sync();
+    if (!*abort) {
+      const int mb = t_first % a.tiles_m, nb = t_first / a.tiles_m;
+      const int r0 = split * kBM / ks, r1 = (split + 1) * kBM / ks;
+      constexpr int kQuads = BN / 4;
+      const float* part = reinterpret_cast<const float*>(smem);
+      for (int i = threadIdx.x; i < (r1 - r0) * kQuads; i += kThreads) {
+        const int rr = r0 + i / kQuads, c4 = (i % kQuads) * 4;
+        const int row = mb * kBM + rr;
+        const float* src = part + rr * (BN + 4) + c4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < ks; ++q) {
+          const float4 v = ld_shared_cluster_v4(map_shared_rank(src, static_cast<uint32_t>(q)));
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+        if (row < a.M) {
+          const __half2 h0 = __floats2half2_rn(acc.x, acc.y), h1 = __floats2half2_rn(acc.z, acc.w);
+          *reinterpret_cast<uint2*>(a.y + static_cast<int64_t>(row) * a.y_ld + nb * BN + c4) =
+              make_uint2(h2_as_u32(h0), h2_as_u32(h1));
+        }
+      }
+    }
+    cluster_sync();  // keep every CTA's partial alive until all remote reads are done
+  }
   if (warp == 1) {
     __syncwarp();
     tc_fence_after_sync();
@@ -321,7 +368,7 @@ int g_gemm_impl = 0;  // 0 auto, 1 chunked decode GEMV, 2 tcgen05, 3 tcgen05 one
 template <int BN>
 int launch_gemm_tc(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz, int64_t qz_ld,
                    const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K, int G, int sm_count,
-                   cudaStream_t stream) {
+                   int ksplit, cudaStream_t stream) {
   using L = Smem<BN>;
   GemmArgs a;
   a.y = y;
@@ -334,6 +381,7 @@ int launch_gemm_tc(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_
   a.tiles_n = N / BN;
   a.num_kb = K / kBK;
   a.gps = G >= kBK ? 1 : kBK / G;
+  a.ksplit = ksplit;
   GemmMaps maps;
   int rc = encode_tensor_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<__half*>(x), K, M,
                                 static_cast<uint64_t>(x_ld) * 2, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -361,12 +409,19 @@ int launch_gemm_tc(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_
   }
   const int tiles = a.tiles_m * a.tiles_n;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(std::min(tiles, sm_count));
+  cfg.gridDim = dim3(ksplit > 1 ? tiles * ksplit : std::min(tiles, sm_count));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   int n = 0;
+  if (ksplit > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = ksplit;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
   if (pdl_enabled()) {
     attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[n].val.programmaticStreamSerializationAllowed = 1;
@@ -395,18 +450,26 @@ int gemm_tc_pair_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_
 int gemm_tc_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz, int64_t qz_ld,
                    const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K, int G, int sm_count,
                    cudaStream_t stream) {
-  // CTA pairs (cta_group::2) once M spans two 128-row tiles and N % 256 == 0:
-  // each SM then writes and feeds the tensor core half as much of the fp16
-  // weight tile, which bounds the one-CTA kernel (shared-memory bandwidth).
+  // CTA pairs (cta_group::2) once M spans two 128-row tiles, N % 256 == 0 and
+  // the pair tiles fill most of the SM pairs: each SM then writes and feeds
+  // the tensor core half as much of the fp16 weight tile, which bounds the
+  // one-CTA kernel (shared-memory bandwidth).
   const bool pair_ok = gemm_tc_pair_eligible(M, N);
+  const int pair_tiles = pair_ok ? ceil_div(M, 2 * kBM) * (N / 256) : 0;
   if (g_gemm_impl == 4 && !pair_ok) return ASHQK_ERR_UNSUPPORTED;
-  if (pair_ok && g_gemm_impl != 3)
+  if (g_gemm_impl == 4 || (pair_ok && g_gemm_impl != 3 && 2 * pair_tiles >= sm_count))
     return gemm_tc_pair_launch(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G, sm_count, stream);
-  // 256-column tiles unless that leaves most SMs idle and 128 columns divide N.
+  // One CTA per tile: 256-column tiles unless that leaves most SMs idle and 128
+  // columns divide N; with fewer tiles than half the SMs, split K over a
+  // cluster (at most 8 CTAs, at least 4 k blocks each).
   const int tiles256 = N % 256 == 0 ? ceil_div(M, kBM) * (N / 256) : 0;
-  if (tiles256 > 0 && (tiles256 >= sm_count || N % 128 != 0))
-    return launch_gemm_tc<256>(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G, sm_count, stream);
-  return launch_gemm_tc<128>(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G, sm_count, stream);
+  const bool wide = tiles256 > 0 && (tiles256 >= sm_count || N % 128 != 0);
+  const int tiles = wide ? tiles256 : ceil_div(M, kBM) * (N / 128);
+  int ks = 1;
+  if (2 * tiles <= sm_count) ks = std::max(1, std::min({8, sm_count / tiles, (K / kBK) / 4}));
+  if (wide)
+    return launch_gemm_tc<256>(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G, sm_count, ks, stream);
+  return launch_gemm_tc<128>(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G, sm_count, ks, stream);
 }
 
 int gemm_impl() { return g_gemm_impl; }

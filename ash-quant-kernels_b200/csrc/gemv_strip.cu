@@ -14,11 +14,12 @@
 // flight per SM: a 64 KB ring lets one SM stream ~49 GB/s, and layers with few
 // column strips need more than that per SM.
 //
-// Warps: one producer (lane 0 issues all TMA loads) and C consumer warps. Stage
-// i belongs to consumer warp i % C, which runs all 16 of its 16-row steps with
-// no further synchronisation and keeps one quantization group for G/16 steps.
-// When the ring is smaller than the CTA's stage count it holds a multiple of C
-// slots, so each slot serves a single warp (phase parities never alias).
+// Warps: one producer (lane 0 issues all TMA loads) and C consumer warps. Ring
+// slot j belongs to consumer warp j % C, which consumes every stage that lands
+// in it, in order -- so no warp waits on a slot whose previous fill belongs to
+// another warp (mbarrier phase parities never alias) -- and runs all 16 of a
+// stage's 16-row steps with no further synchronisation, keeping one
+// quantization group for G/16 steps.
 // A lane unpacks one word (8 columns) of rows {2t, 2t+1, 2t+8, 2t+9} per step
 // -- the k order of an mma.sync A fragment -- with the prmt / LOP3 / HSUB2 code
 // of csrc/awq_unpack.cuh, and mma.sync.m16n8k16 accumulates sum x (q - z) per
@@ -185,8 +186,11 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
     };
 
     int grp_end = -1;
-    for (int li = warp; li < nloc; li += C) {
-      const int slot = li % a.ring;
+    // Warp w consumes every fill of the ring slots j with j % C == w, in stage
+    // order, so it never waits on a slot whose previous fill belongs to
+    // another warp and may not have landed (phase parity would alias).
+    for (int li = warp < a.ring ? warp : nloc, round = 0; li < nloc;) {  // a warp past the ring owns no slot
+      const int slot = li - round;  // round = the first stage of this pass over the ring
       if (!mbar_wait(&full[slot], (li / a.ring) & 1, &abort_flag)) break;
       const uint32_t base = smem_s + slot * a.stage_bytes;
       const int k0 = (sb + li) * kBoxRows;
@@ -237,6 +241,12 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
+      // Next slot of this warp (j += C); past the ring's end, the next pass.
+      li += C;
+      if (li - round >= a.ring) {
+        round += a.ring;
+        li = round + warp;
+      }
     }
     if (cur_grp >= 0) flush();
   }
@@ -359,16 +369,9 @@ bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p) {
   ring = std::min(ring, kMaxStages);
   const int local = ceil_div(p->stages_total, p->ksplit);
   ring = std::min(ring, std::max(local, 1));
-  if (ring < local) {
-    // Slots are reused. A consumer warp tells a slot's fills apart only by
-    // mbarrier phase parity, so it must never wait on a slot whose previous
-    // fill has not landed yet: that happens when another warp's stage sits in
-    // the slot. With ring a multiple of C, slot j only ever holds the stages
-    // of warp j % C, which that warp consumes in order.
-    while (p->consumers > 4 && ring < p->consumers) p->consumers /= 2;
-    ring = ring / p->consumers * p->consumers;
-    if (ring < p->consumers) return false;
-  }
+  // Slots are owned by warps (slot j by warp j % C); with fewer slots than
+  // warps the extra warps would idle, so shrink C first.
+  while (p->consumers > 4 && ring < p->consumers) p->consumers /= 2;
   p->ring = std::max(ring, 1);
   const size_t red = static_cast<size_t>(p->consumers) * (M > 8 ? 16 : 8) * (kStripCols + 4) * 4 +
                      static_cast<size_t>(M) * kStripCols * 4;
@@ -428,7 +431,6 @@ int gemv_strip_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t 
                       int sm_count, cudaStream_t stream) {
   StripPlan p;
   if (!plan_strip(M, N, K, G, sm_count, &p)) return ASHQK_ERR_UNSUPPORTED;
-  if (p.ring < ceil_div(p.stages_total, p.ksplit) && p.ring % p.consumers != 0) return ASHQK_ERR_UNSUPPORTED;
   StripMaps maps;
   int rc = encode_tensor_map_2d(&maps.qw, CU_TENSOR_MAP_DATA_TYPE_INT32, const_cast<int32_t*>(qw), N / 8, K,
                                 static_cast<uint64_t>(qw_ld) * 4, kStripWords, kBoxRows, CU_TENSOR_MAP_SWIZZLE_NONE);

@@ -247,6 +247,12 @@ __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
   return v;
 }
 
+__device__ __forceinline__ float4 ld_shared_cluster_v4(uint32_t addr) {
+  float4 v;
+  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
 // ---- programmatic dependent launch -------------------------------------------
 
 // Block until the grid this launch depends on has completed and its writes are
