@@ -484,6 +484,7 @@ def run_gpu(args):
         with torch.cuda.graph(g):
             out = stack_step(stack, h, world, group)
         graphs[m] = (g, h, out)
+        del g  # the dict holds the only reference (graphs with NCCL calls must be freed before teardown)
 
     g1, h1, out1 = graphs[1]
     with ClockSampler(local) as clocks:
@@ -523,8 +524,11 @@ def run_gpu(args):
     prefill = prefill_gemm(PREFILL_M, 10, warmup, torch, tensor_peak) if world == 1 and args.only == "all" else None
     tp_res = tp_mlp(world, rank, group, 10, warmup, torch, dist) if args.only == "all" else None
 
+    # Every CUDA graph that captured NCCL calls is released before the process
+    # group is destroyed; a live one makes destroy_process_group wait forever.
+    del g1, h1, out1
     graphs.clear()
-    del g1, out1
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
