@@ -333,17 +333,18 @@ bool half_sm_budget() {
   return on;
 }
 
-// CTAs per SM a K split may reach: 3 for deep layers (>= 32 stages, K >= 8192:
-// measured 14.1 -> 13.6 us on 4096 x 12288), else 1 (shallower layers lose
-// more to sharing SMs than they gain). Env ASHQK_STRIP_SPLIT_LIMIT overrides.
-int split_limit(int stages_total) {
+// CTAs per SM a K split may reach: 3 for deep layers at M <= 8 (>= 32 stages,
+// K >= 8192: measured 14.1 -> 13.6 us on 4096 x 12288 at M=1), else 1
+// (shallower layers, and M > 8 with its twice larger stages, lose more to
+// sharing SMs than they gain). Env ASHQK_STRIP_SPLIT_LIMIT overrides.
+int split_limit(int M, int stages_total) {
   static const int v = [] {
     const char* e = std::getenv("ASHQK_STRIP_SPLIT_LIMIT");
     const int x = e ? std::atoi(e) : 0;
     return x >= 1 && x <= 4 ? x : 0;
   }();
   if (v) return v;
-  return stages_total >= 32 ? 3 : 1;
+  return (M <= 8 && stages_total >= 32) ? 3 : 1;
 }
 
 bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p) {
@@ -360,7 +361,7 @@ bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p) {
   // within split_limit per SM; wide layers (more strips than SMs) are not split.
   p->ksplit = 1;
   for (int ks = 4; ks >= 2; --ks)
-    if (p->tiles * ks <= split_limit(p->stages_total) * sm_count && ks <= p->stages_total) {
+    if (p->tiles * ks <= split_limit(M, p->stages_total) * sm_count && ks <= p->stages_total) {
       p->ksplit = ks;
       break;
     }
