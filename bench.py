@@ -403,6 +403,76 @@ def prefill_gemm(ms, reps, warmup, torch, tensor_peak):
     return res
 
 
+def marlin_compare(torch, reps=3):
+    """The reference's real bar (its results/v0.2-vs-marlin-findings.md): vLLM's AWQ-Marlin
+    kernel on the same B200, as a black box through vLLM's own conversion helpers. Per layer
+    type: a CUDA graph of 36 launches over 36 distinct converted weight sets at M=1, like the
+    per-layer GEMV timing; prefill gate_up / down at M=2048 with the L2 flushed; and the
+    relative difference of Marlin's output from ours on one layer (both fp32-accumulated)."""
+    try:
+        from vllm import _custom_ops as vops
+        from vllm.model_executor.layers.quantization.utils import marlin_utils as mu
+        from vllm.scalar_type import scalar_types
+    except Exception as e:  # vLLM absent or unusable here
+        return {"unavailable": f"vllm import failed: {type(e).__name__}: {e}"[:300]}
+    from ashqk import w4a16_linear
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+
+    def convert(qw, qz, s, n, k):
+        return (vops.awq_marlin_repack(qw, size_k=k, size_n=n, num_bits=4),
+                mu.marlin_permute_scales(s, size_k=k, size_n=n, group_size=GROUP),
+                mu.awq_to_marlin_zero_points(qz, size_k=k // GROUP, size_n=n, num_bits=4))
+
+    g_idx = mu.marlin_make_empty_g_idx(dev)
+    perm = mu.marlin_make_empty_g_idx(dev)
+    ws = mu.marlin_make_workspace_new(dev)
+
+    def marlin(x, w, n, k):
+        return mu.apply_awq_marlin_linear(x, w[0], w[1], w[2], g_idx, perm, ws, scalar_types.uint4, n, k)
+
+    res = {"kernel": "vLLM awq_marlin (marlin_gemm), weights converted with vLLM's helpers", "per_layer_m1_us": {}}
+    try:
+        for j, (name, n, k) in enumerate(LAYERS):
+            sets = [convert(*random_awq(n, k, 500 + 10 * j + i, dev, torch), n, k) for i in range(N_LAYERS)]
+            x = torch.randn(1, k, device=dev).half()
+            marlin(x, sets[0], n, k)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for w in sets:
+                    marlin(x, w, n, k)
+            for _ in range(2):
+                g.replay()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(reps):
+                g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            res["per_layer_m1_us"][name] = round(a.elapsed_time(b) * 1e3 / (reps * N_LAYERS), 2)
+            del g, sets
+        res["stack_us_per_token_est"] = round(N_LAYERS * sum(res["per_layer_m1_us"].values()), 1)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        res["prefill_m2048"] = {}
+        for j, (name, n, k) in enumerate(PREFILL_LAYERS):
+            qw, qz, s = random_awq(n, k, 900 + j, dev, torch)
+            w = convert(qw, qz, s, n, k)
+            x = torch.randn(2048, k, device=dev).half()
+            us = time_flushed(lambda: marlin(x, w, n, k), 10, 3, torch, flush)
+            res["prefill_m2048"][name] = {"us": round(us, 1), "tflops": round(2.0 * 2048 * n * k / us / 1e6, 1)}
+            if j == 0:
+                y_ref = w4a16_linear(x, qw, qz, s).float()
+                y_m = marlin(x, w, n, k).float()
+                res["rel_diff_vs_ours_gate_up_m2048"] = float((y_m - y_ref).norm() / y_ref.norm())
+        del flush
+    except Exception as e:
+        res["error"] = f"{type(e).__name__}: {e}"[:300]
+    torch.cuda.empty_cache()
+    return res
+
+
 def tp_mlp(world, rank, group, reps, warmup, torch, dist):
     """a large dense MLP under tensor parallelism (gate_up K=8192 N=57344
     column-parallel + NCCL all-gather; down K=28672 N=8192 row-parallel + all-reduce), per M:
@@ -523,6 +593,7 @@ def run_gpu(args):
     torch.cuda.empty_cache()
     prefill = prefill_gemm(PREFILL_M, 10, warmup, torch, tensor_peak) if world == 1 and args.only == "all" else None
     tp_res = tp_mlp(world, rank, group, 10, warmup, torch, dist) if args.only == "all" else None
+    marlin_res = marlin_compare(torch) if world == 1 and args.only == "all" and not args.no_marlin else None
 
     # Every CUDA graph that captured NCCL calls is released before the process
     # group is destroyed; a live one makes destroy_process_group wait forever.
@@ -572,6 +643,8 @@ def run_gpu(args):
             "config": "gate_up K=8192 N=57344 column-parallel + all-gather, down K=28672 N=8192 row-parallel + "
                       f"all-reduce, G=128, tp{world}, max over ranks", "per_m": tp_res,
         }
+    if marlin_res is not None:
+        line["marlin_vllm"] = marlin_res
     if layer_bw is not None:
         tot_bytes = sum(w4a16_bytes(1, n, k, GROUP) for _, n, k in LAYERS)
         tot_us = sum(layer_bw[nm]["us"] for nm, _, _ in LAYERS)
@@ -623,6 +696,7 @@ def main():
     ap.add_argument("--only", choices=["all", "decode", "prefill"], default="all",
                     help="decode: the decode stack alone; prefill: only the prefill GEMM (profiling runs)")
     ap.add_argument("--prefill-m", type=int, nargs="*", default=None, help="M values for --only prefill")
+    ap.add_argument("--no-marlin", action="store_true", help="skip the vLLM Marlin comparison")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="decoder layers in the stack (36 is the benchmark; fewer for profiling runs)")
     args = ap.parse_args()
