@@ -403,6 +403,43 @@ def prefill_gemm(ms, reps, warmup, torch, tensor_peak):
     return res
 
 
+# The reference's default benchmark model (its bench/shapes.py): Qwen3.5-9B, 32 decoder layers in a
+# 3:1 pattern of linear-attention and full-attention layers (name, N, K, layer count).
+QWEN35_LAYERS = (("in_proj_qkvz", 12288, 4096, 24), ("in_proj_ba", 64, 4096, 24), ("out_proj", 4096, 4096, 24),
+                 ("qkv_proj", 10240, 4096, 8), ("o_proj", 4096, 4096, 8), ("gate_up_proj", 24576, 4096, 32),
+                 ("down_proj", 4096, 12288, 32))
+
+
+def qwen35_stack(torch, steps, warmup):
+    """All linear layers of one Qwen3.5-9B token at M=1 (distinct weights per layer, one CUDA graph,
+    each call fed a fixed input of its K); us/token and algorithmic GB/s."""
+    from ashqk import w4a16_linear
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    layers = []
+    for j, (name, n, k, count) in enumerate(QWEN35_LAYERS):
+        for i in range(count):
+            layers.append((n, k) + random_awq(n, k, 2000 + 100 * j + i, dev, torch))
+    xs = {k: torch.randn(1, k, device=dev).half() for _, _, k, _ in QWEN35_LAYERS}
+
+    def step():
+        for n, k, qw, qz, s in layers:
+            w4a16_linear(xs[k], qw, qz, s)
+
+    step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    ms = time_graph(g, steps, warmup, torch, None, 1)
+    nbytes = sum(w4a16_bytes(1, n, k, GROUP) for n, k, _, _, _ in layers)
+    del g, layers
+    torch.cuda.empty_cache()
+    return {"model": "qwen3.5-9b linear layers (random AWQ weights, G=128), M=1",
+            "launches": sum(c for *_, c in QWEN35_LAYERS), "us_per_token": round(ms * 1e3, 1),
+            "hbm_gbs": round(nbytes / (ms * 1e-3) / 1e9, 1), "bytes_per_token": nbytes}
+
+
 def marlin_compare(torch, reps=3):
     """The reference's real bar (its results/v0.2-vs-marlin-findings.md): vLLM's AWQ-Marlin
     kernel on the same B200, as a black box through vLLM's own conversion helpers. Per layer
@@ -593,6 +630,7 @@ def run_gpu(args):
     torch.cuda.empty_cache()
     prefill = prefill_gemm(PREFILL_M, 10, warmup, torch, tensor_peak) if world == 1 and args.only == "all" else None
     tp_res = tp_mlp(world, rank, group, 10, warmup, torch, dist) if args.only == "all" else None
+    q35 = qwen35_stack(torch, max(args.steps // 2, 10), warmup) if world == 1 and args.only == "all" else None
     marlin_res = marlin_compare(torch) if world == 1 and args.only == "all" and not args.no_marlin else None
 
     # Every CUDA graph that captured NCCL calls is released before the process
@@ -643,6 +681,8 @@ def run_gpu(args):
             "config": "gate_up K=8192 N=57344 column-parallel + all-gather, down K=28672 N=8192 row-parallel + "
                       f"all-reduce, G=128, tp{world}, max over ranks", "per_m": tp_res,
         }
+    if q35 is not None:
+        line["qwen35_9b_stack"] = q35
     if marlin_res is not None:
         line["marlin_vllm"] = marlin_res
     if layer_bw is not None:
