@@ -420,24 +420,29 @@ def qwen35_stack(torch, steps, warmup):
     for j, (name, n, k, count) in enumerate(QWEN35_LAYERS):
         for i in range(count):
             layers.append((n, k) + random_awq(n, k, 2000 + 100 * j + i, dev, torch))
-    xs = {k: torch.randn(1, k, device=dev).half() for _, _, k, _ in QWEN35_LAYERS}
+    res = {"model": "qwen3.5-9b linear layers (random AWQ weights, G=128)",
+           "launches": sum(c for *_, c in QWEN35_LAYERS),
+           "reference_h200_published_us_per_token": {"m1": {"ashqk": 3325, "marlin": 1990, "fp16": 3886},
+                                                     "m4": {"ashqk": 5580, "marlin": 2002, "fp16": 3899}}}
+    for m in (1, 4):
+        xs = {k: torch.randn(m, k, device=dev).half() for _, _, k, _ in QWEN35_LAYERS}
 
-    def step():
-        for n, k, qw, qz, s in layers:
-            w4a16_linear(xs[k], qw, qz, s)
+        def step():
+            for n, k, qw, qz, s in layers:
+                w4a16_linear(xs[k], qw, qz, s)
 
-    step()
-    torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
         step()
-    ms = time_graph(g, steps, warmup, torch, None, 1)
-    nbytes = sum(w4a16_bytes(1, n, k, GROUP) for n, k, _, _, _ in layers)
-    del g, layers
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        ms = time_graph(g, steps, warmup, torch, None, 1)
+        nbytes = sum(w4a16_bytes(m, n, k, GROUP) for n, k, _, _, _ in layers)
+        res[f"m{m}"] = {"us_per_step": round(ms * 1e3, 1), "hbm_gbs": round(nbytes / (ms * 1e-3) / 1e9, 1)}
+        del g
+    del layers
     torch.cuda.empty_cache()
-    return {"model": "qwen3.5-9b linear layers (random AWQ weights, G=128), M=1",
-            "launches": sum(c for *_, c in QWEN35_LAYERS), "us_per_token": round(ms * 1e3, 1),
-            "hbm_gbs": round(nbytes / (ms * 1e-3) / 1e9, 1), "bytes_per_token": nbytes}
+    return res
 
 
 def marlin_compare(torch, reps=3):
