@@ -51,6 +51,7 @@ struct GemmArgs {
   int64_t y_ld;
   int M, N, K, G;
   int tiles_m, tiles_n, num_kb, gps;
+  int n_fastest;  // tile order: 1 = consecutive tiles walk N (x block stays in L2), 0 = walk M
   int ksplit;  // > 1: a cluster of ksplit CTAs shares one tile's K range (one tile per cluster)
 };
 
@@ -76,6 +77,12 @@ struct Smem {
   static_assert(off_b % 1024 == 0 && kX % 1024 == 0 && kB % 1024 == 0, "swizzle atoms need 1 KB alignment");
   static_assert(off_bar % 8 == 0, "mbarriers need 8-byte alignment");
 };
+
+// Tile t -> (row block, column block). Tiles that run at the same time share
+// their row block of x when N is walked first (x larger than the weights: the
+// weights stay in L2 and x is read once), or their weight columns otherwise.
+__device__ __forceinline__ int tile_m(const GemmArgs& a, int t) { return a.n_fastest ? t / a.tiles_n : t % a.tiles_m; }
+__device__ __forceinline__ int tile_n(const GemmArgs& a, int t) { return a.n_fastest ? t % a.tiles_n : t / a.tiles_m; }
 
 __device__ __forceinline__ void sts_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
@@ -153,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       for (int t = t_first; t < tiles; t += t_step) {
-        const int mb = t % a.tiles_m, nb = t / a.tiles_m;
+        const int mb = tile_m(a, t), nb = tile_n(a, t);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_a[stage], phase ^ 1u, abort, true)) break;
           mbar_arrive_expect_tx(&full_a[stage], tx);
@@ -230,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t pacc = 0;
     for (int t = t_first; t < tiles; t += t_step) {
-      const int mb = t % a.tiles_m, nb = t / a.tiles_m;
+      const int mb = tile_m(a, t), nb = tile_n(a, t);
       if (!mbar_wait(&acc_full[acc], pacc, abort)) break;
       tc_fence_after_sync();
       const int row = mb * kBM + 32 * quad + lane;
@@ -331,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // tile and adds the ranks' partials in fixed order (deterministic).
     cluster_sync();
     if (!*abort) {
-      const int mb = t_first % a.tiles_m, nb = t_first / a.tiles_m;
+      const int mb = tile_m(a, t_first), nb = tile_n(a, t_first);
       const int r0 = split * kBM / ks, r1 = (split + 1) * kBM / ks;
       constexpr int kQuads = BN / 4;
       const float* part = reinterpret_cast<const float*>(smem);
@@ -381,6 +388,8 @@ int launch_gemm_tc(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_
   a.tiles_n = N / BN;
   a.num_kb = K / kBK;
   a.gps = G >= kBK ? 1 : kBK / G;
+  // x bytes vs packed weight bytes: keep the smaller operand resident in L2.
+  a.n_fastest = static_cast<int64_t>(M) * K * 2 > static_cast<int64_t>(K) * N / 2 ? 1 : 0;
   a.ksplit = ksplit;
   GemmMaps maps;
   int rc = encode_tensor_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<__half*>(x), K, M,

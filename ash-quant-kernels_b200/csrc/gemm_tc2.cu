@@ -48,6 +48,7 @@ struct PairArgs {
   int64_t y_ld;
   int M, N, K, G;
   int tiles_m, tiles_n, num_kb, gps;  // tiles_m counts 256-row pair tiles
+  int n_fastest;  // tile order: 1 = consecutive tiles walk N (x block stays in L2), 0 = walk M
 };
 
 struct PairSmem {
@@ -71,6 +72,12 @@ struct PairSmem {
   static_assert(off_b % 1024 == 0 && kX % 1024 == 0 && kB % 1024 == 0, "swizzle atoms need 1 KB alignment");
   static_assert(off_q % 128 == 0 && off_s % 128 == 0 && off_z % 128 == 0, "TMA destinations need 128 B alignment");
 };
+
+// Tile t -> (row block, column block). Tiles that run at the same time share
+// their row block of x when N is walked first (x larger than the weights: the
+// weights stay in L2 and x is read once), or their weight columns otherwise.
+__device__ __forceinline__ int tile_m(const PairArgs& a, int t) { return a.n_fastest ? t / a.tiles_n : t % a.tiles_m; }
+__device__ __forceinline__ int tile_n(const PairArgs& a, int t) { return a.n_fastest ? t % a.tiles_n : t / a.tiles_m; }
 
 __device__ __forceinline__ void sts_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
@@ -143,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0, issued = 0;
       uint32_t phase = 0;
       for (int t = pair; t < tiles && !*abort; t += pairs) {
-        const int mp = t % a.tiles_m, nb = t / a.tiles_m;
+        const int mp = tile_m(a, t), nb = tile_n(a, t);
         const int row0 = mp * (2 * kBM) + static_cast<int>(rank) * kBM;
         const int col0 = nb * kBN + static_cast<int>(rank) * kHalfN;
         for (int kb = 0; kb < a.num_kb; ++kb) {
@@ -216,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t pacc = 0;
     for (int t = pair; t < tiles; t += pairs) {
-      const int mp = t % a.tiles_m, nb = t / a.tiles_m;
+      const int mp = tile_m(a, t), nb = tile_n(a, t);
       if (!mbar_wait(&acc_full[acc], pacc, abort)) break;
       tc_fence_after_sync();
       const int row = mp * (2 * kBM) + static_cast<int>(rank) * kBM + 32 * quad + lane;
@@ -333,6 +340,8 @@ int gemm_tc_pair_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_
   a.tiles_n = N / kBN;
   a.num_kb = K / kBK;
   a.gps = G >= kBK ? 1 : kBK / G;
+  // x bytes vs packed weight bytes: keep the smaller operand resident in L2.
+  a.n_fastest = static_cast<int64_t>(M) * K * 2 > static_cast<int64_t>(K) * N / 2 ? 1 : 0;
   PairMaps maps;
   int rc = encode_tensor_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<__half*>(x), K, M,
                                 static_cast<uint64_t>(x_ld) * 2, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
