@@ -333,6 +333,24 @@ bool half_sm_budget() {
   return on;
 }
 
+// Tuning knobs for the co-residency experiments (env; 0 = unset).
+int smem_cap_kb() {
+  static const int v = [] {
+    const char* e = std::getenv("ASHQK_STRIP_SMEM_CAP_KB");
+    const int x = e ? std::atoi(e) : 0;
+    return x >= 32 && x <= 224 ? x : 0;
+  }();
+  return v;
+}
+int max_consumers() {
+  static const int v = [] {
+    const char* e = std::getenv("ASHQK_STRIP_MAX_C");
+    const int x = e ? std::atoi(e) : 0;
+    return x == 4 || x == 8 || x == 16 ? x : 0;
+  }();
+  return v;
+}
+
 // CTAs per SM a K split may reach: 3 for deep layers at M <= 8 (>= 32 stages,
 // K >= 8192: measured 14.1 -> 13.6 us on 4096 x 12288 at M=1), else 1
 // (shallower layers, and M > 8 with its twice larger stages, lose more to
@@ -375,9 +393,13 @@ bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p) {
     p->consumers = 16;
   else
     p->consumers = 8;
-  // With half_sm, a CTA takes at most half an SM's shared memory so that the
-  // next kernel's CTAs (programmatic dependent launch) can be resident beside it.
-  const size_t cap = half_sm_budget() ? 110 * 1024 : 224 * 1024;
+  // With half_sm (or an explicit cap), a CTA takes at most that much shared
+  // memory so that the next kernel's CTAs (programmatic dependent launch) can
+  // be resident beside it.
+  const size_t cap = smem_cap_kb() > 0 ? static_cast<size_t>(smem_cap_kb()) * 1024
+                                       : (half_sm_budget() ? 110 * 1024 : 224 * 1024);
+  if (max_consumers() > 0)
+    while (p->consumers > 4 && p->consumers > max_consumers()) p->consumers /= 2;
   const size_t budget = std::min<size_t>(cap, (228 * 1024) / per_sm - 2048) - 1024;
   int ring = static_cast<int>(budget / p->stage_bytes);
   ring = std::min(ring, kMaxStages);
