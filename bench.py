@@ -678,7 +678,9 @@ def run_gpu(args):
         }
     if prefill is not None:
         line["prefill_gemm"] = {
-            "kernel": "gemm_tc_kernel (tcgen05.mma, TMEM accumulators)", "peak_tflops": tensor_peak,
+            "kernel": "gemm_tc_pair_kernel (cta_group::2, when M > 128 and the pair tiles fill half the SMs) / "
+                      "gemm_tc_kernel (one CTA per tile, K split over a cluster when tiles are few); tcgen05.mma "
+                      "with TMEM accumulators", "peak_tflops": tensor_peak,
             "peak_kind": tensor_kind, "l2": "flushed (256 MB write) before every timed call", "shapes": prefill,
         }
     if tp_res is not None:
