@@ -23,6 +23,7 @@
 //
 // Every mbarrier wait is bounded (sm100.cuh); on a timeout the CTA records the
 // device error, all roles stop, and TMEM is released before the kernel exits.
+#include <atomic>
 #include <algorithm>
 
 #include "awq_unpack.cuh"
@@ -406,15 +407,15 @@ int launch_gemm_tc(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_
   if (rc) return rc;
 
   const size_t smem = L::bytes + 1024;  // + alignment slack
-  static bool configured[64] = {};
+  static std::atomic<bool> configured[64];  // zero-initialised (static storage)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ASHQK_ERR_CUDA;
   auto kernel = gemm_tc_kernel<BN>;
-  if (!configured[dev]) {
+  if (!configured[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
       return ASHQK_ERR_CUDA;
-    configured[dev] = true;
+    configured[dev].store(true, std::memory_order_release);
   }
   const int tiles = a.tiles_m * a.tiles_n;
   cudaLaunchConfig_t cfg = {};

@@ -18,6 +18,7 @@
 //
 // Both CTAs allocate TMEM together (cta_group::2) and meet at a cluster barrier
 // before releasing it, after every MMA has completed. All waits are bounded.
+#include <atomic>
 #include <algorithm>
 
 #include "awq_unpack.cuh"
@@ -357,14 +358,14 @@ int gemm_tc_pair_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_
   if (rc) return rc;
 
   const size_t smem = L::bytes + 1024;
-  static bool configured[64] = {};
+  static std::atomic<bool> configured[64];  // zero-initialised (static storage)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ASHQK_ERR_CUDA;
-  if (!configured[dev]) {
+  if (!configured[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(gemm_tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
       return ASHQK_ERR_CUDA;
-    configured[dev] = true;
+    configured[dev].store(true, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(kThreads);
@@ -380,18 +381,18 @@ int gemm_tc_pair_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_
   // The kernel is persistent, so every pair must be resident at once: a pair
   // left for a second wave would start its whole share of tiles late. Pairs
   // need two free SMs in one GPC, so fewer than sm_count / 2 may fit.
-  static int resident_pairs[64] = {};
-  if (resident_pairs[dev] == 0) {
+  static std::atomic<int> resident_pairs[64];  // zero-initialised (static storage)
+  if (resident_pairs[dev].load(std::memory_order_acquire) == 0) {
     cfg.gridDim = dim3(2 * (sm_count / 2));
     cfg.attrs = attr;
     cfg.numAttrs = n;
     int clusters = 0;
     if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_pair_kernel, &cfg) != cudaSuccess || clusters <= 0)
       return ASHQK_ERR_CUDA;
-    resident_pairs[dev] = std::min(clusters, sm_count / 2);
+    resident_pairs[dev].store(std::min(clusters, sm_count / 2), std::memory_order_release);
   }
   const int tiles = a.tiles_m * a.tiles_n;
-  const int pairs = std::min(tiles, resident_pairs[dev]);
+  const int pairs = std::min(tiles, resident_pairs[dev].load(std::memory_order_acquire));
   cfg.gridDim = dim3(2 * pairs);
   if (pdl_enabled()) {
     attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -24,6 +24,7 @@
 //  * Split-K partials go to fp32 slots of a caller-owned workspace; the last
 //    CTA of a column tile sums the slots in fixed order (deterministic), writes
 //    fp16 y and resets the tile's arrival counter.
+#include <atomic>
 #include <algorithm>
 
 #include "awq_unpack.cuh"
@@ -351,14 +352,14 @@ int plan_gemv(int M, int N, int K, int G, int split_req, int sm_count, Plan* p) 
 
 template <int MT, bool VEC>
 int launch_instance(const GemvArgs& args, const Plan& p, cudaStream_t stream) {
-  static bool configured[64] = {};  // per template instance and device
+  static std::atomic<bool> configured[64];  // zero-initialised (static storage)  // per template instance and device
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ASHQK_ERR_CUDA;
-  if (!configured[dev]) {
+  if (!configured[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(gemv_kernel<MT, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
         cudaSuccess)
       return ASHQK_ERR_CUDA;
-    configured[dev] = true;
+    configured[dev].store(true, std::memory_order_release);
   }
   gemv_kernel<MT, VEC><<<dim3(p.tiles, p.splits), kThreads, p.smem, stream>>>(args);
   return launch_status();

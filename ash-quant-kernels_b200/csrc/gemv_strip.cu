@@ -29,6 +29,7 @@
 // Programmatic dependent launch: weights, scales and zeros of the first ring
 // stages are requested before griddepcontrol.wait; x (the previous kernel's
 // output) after it; y is written only after it.
+#include <atomic>
 #include <algorithm>
 #include <cstdlib>
 
@@ -418,16 +419,16 @@ bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p) {
 template <int MT, int C>
 int launch_strip(const StripMaps& maps, const StripArgs& args, int tiles, size_t smem, cudaStream_t stream) {
   const int ks = args.ksplit;
-  static bool configured[64] = {};
+  static std::atomic<bool> configured[64];  // zero-initialised (static storage)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ASHQK_ERR_CUDA;
   auto kernel = gemv_strip_kernel<MT, C>;
-  if (!configured[dev]) {
+  if (!configured[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared) != cudaSuccess)
       return ASHQK_ERR_CUDA;
-    configured[dev] = true;
+    configured[dev].store(true, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles, ks);

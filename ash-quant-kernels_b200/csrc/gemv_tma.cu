@@ -28,6 +28,7 @@
 //    previous kernel's output), y and the workspace are touched after
 //    griddepcontrol.wait, so the next layer's weights stream during this
 //    layer's tail.
+#include <atomic>
 #include <algorithm>
 #include <cstdlib>
 
@@ -491,18 +492,18 @@ void plan_tma(int M, int N, int K, int G, int split_req, int sm_count, TmaPlan* 
 
 template <int MT, bool CLUSTER>
 int launch_tma(const CUtensorMap& map, const TmaGemvArgs& args, const TmaPlan& p, cudaStream_t stream) {
-  static bool configured[64] = {};
+  static std::atomic<bool> configured[64];  // zero-initialised (static storage)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ASHQK_ERR_CUDA;
   auto kernel = gemv_tma_kernel<MT, CLUSTER>;
-  if (!configured[dev]) {
+  if (!configured[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimitOneCta) != cudaSuccess ||
         cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared) != cudaSuccess)
       return ASHQK_ERR_CUDA;
     if (CLUSTER && cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
       return ASHQK_ERR_CUDA;
-    configured[dev] = true;
+    configured[dev].store(true, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.tiles, p.splits);

@@ -67,16 +67,14 @@ __global__ void __launch_bounds__(32) l2_prefetch_kernel(Region qw, Region qz, R
   pdl_wait();  // complete only after the kernel before it: the next launch relies on that
 }
 
-int g_prefetch = -1;  // -1: read ASHQK_L2_PREFETCH once
-
 }  // namespace
 
 bool l2_prefetch_enabled() {
-  if (g_prefetch < 0) {
+  static const bool on = [] {  // read once (thread-safe static initialisation)
     const char* e = std::getenv("ASHQK_L2_PREFETCH");
-    g_prefetch = (e && e[0] == '1') ? 1 : 0;
-  }
-  return g_prefetch == 1;
+    return e && e[0] == '1';
+  }();
+  return on;
 }
 
 // Launch the prefetch of one layer's AWQ tensors on `stream` (programmatic
