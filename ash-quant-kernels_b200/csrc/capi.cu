@@ -19,7 +19,12 @@ std::mutex g_info_mu;
 
 int device_info(DeviceInfo* out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return ASHQK_ERR_CUDA;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) {
+    cudaGetLastError();  // clear the sticky-free error so later calls start clean
+    return ASHQK_ERR_NO_DEVICE;
+  }
+  if (e != cudaSuccess) return ASHQK_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return ASHQK_ERR_NO_DEVICE;
   std::lock_guard<std::mutex> lock(g_info_mu);
   DeviceInfo& d = g_info[dev];

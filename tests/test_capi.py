@@ -64,3 +64,30 @@ def test_invalid_arguments_rejected_before_launch(lib):
     assert f(fake, 100, fake, 8, fake, 8, fake, 64, fake, 64, 1, 64, 256, 128, None, 0, None) == 1
     sz = ctypes.c_size_t(0)
     assert lib.ashqk_linear_workspace_size(1, 60, 256, 128, ctypes.byref(sz)) == 1
+
+
+def test_kernel_switches_validate_their_argument(lib):
+    """Test and tuning switches: out-of-range choices are refused, valid ones accepted (no GPU touched)."""
+    for which in (0, 1, 2, 3):
+        assert lib.ashqk_set_gemv_kernel(which) == 0
+    assert lib.ashqk_set_gemv_kernel(4) == 1 and lib.ashqk_set_gemv_kernel(-1) == 1
+    for which in (0, 1, 2, 3, 4):
+        assert lib.ashqk_set_gemm_kernel(which) == 0
+    assert lib.ashqk_set_gemm_kernel(5) == 1 and lib.ashqk_set_gemm_kernel(-1) == 1
+    assert lib.ashqk_set_gemv_kernel(0) == 0 and lib.ashqk_set_gemm_kernel(0) == 0
+
+
+def test_workspace_size_queries(lib):
+    """Malformed problems are refused before the device is consulted; a well-formed query needs the
+    GPU's SM count, so without a B200 it reports ASHQK_ERR_NO_DEVICE (5), never a size."""
+    sz = ctypes.c_size_t(123)
+    lib.ashqk_gemm_workspace_size.argtypes = [ctypes.c_int] * 4 + [ctypes.POINTER(ctypes.c_size_t)]
+    assert lib.ashqk_gemm_workspace_size(0, 24576, 4096, 128, ctypes.byref(sz)) == 1
+    assert lib.ashqk_gemm_workspace_size(16, 24576, 4000, 128, ctypes.byref(sz)) == 1
+    lib.ashqk_gemv_workspace_size.argtypes = [ctypes.c_int] * 5 + [ctypes.POINTER(ctypes.c_size_t)]
+    assert lib.ashqk_gemv_workspace_size(1, 6140, 4096, 128, 0, ctypes.byref(sz)) == 1  # N % 8 != 0
+    import torch
+
+    if not torch.cuda.is_available():
+        assert lib.ashqk_gemm_workspace_size(2048, 24576, 4096, 128, ctypes.byref(sz)) == 5
+        assert lib.ashqk_gemv_workspace_size(1, 6144, 4096, 128, 0, ctypes.byref(sz)) == 5
