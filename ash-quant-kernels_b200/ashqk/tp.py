@@ -111,17 +111,22 @@ def column_parallel_linear(x: torch.Tensor, qweight, qzeros, scales, group=None,
 
 
 def row_parallel_linear(x_local: torch.Tensor, qweight, qzeros, scales, group=None,
-                        reduce_dtype: Optional[torch.dtype] = None, linear: Optional[Linear] = None) -> torch.Tensor:
+                        reduce_dtype: Optional[torch.dtype] = None, linear: Optional[Linear] = None,
+                        allreduce: Optional["P2PAllReduce"] = None) -> torch.Tensor:
     """Partial y = x[..., shard] @ W[shard, :] on every rank, summed over ranks.
 
     ``reduce_dtype=torch.float32`` sums the partials in fp32 (one rounding to
-    fp16 at the end instead of one per reduction step).
+    fp16 at the end instead of one per reduction step). ``allreduce`` (a
+    ``P2PAllReduce`` of the same group) replaces NCCL for partials it can hold;
+    it too sums in fp32 with one rounding.
     """
     linear = linear or w4a16_linear
     y = linear(x_local, qweight, qzeros, scales)
     _, world = _world(group)
     if world == 1:
         return y
+    if allreduce is not None and y.is_contiguous() and y.numel() % 8 == 0 and y.numel() <= allreduce.max_elems:
+        return allreduce(y, out=y)
     if reduce_dtype is not None and reduce_dtype != y.dtype:
         acc = y.to(reduce_dtype)
         dist.all_reduce(acc, group=group)
@@ -168,3 +173,88 @@ class RowParallelW4A16Linear(torch.nn.Module):
         if not self.input_is_parallel:
             x = shard_input(x, self.rank, self.world)
         return row_parallel_linear(x, self.qweight, self.qzeros, self.scales, self.group, self.reduce_dtype)
+
+
+class P2PAllReduce:
+    """Sum of fp16 tensors over the ranks of ``group`` through NVLink peer memory (one CUDA IPC
+    region per rank, a one-CTA kernel per call; ``ashqk_allreduce_f16_oneshot``), for the small
+    row-parallel partials of tensor-parallel decode where NCCL's per-call cost dominates.
+
+    Every rank must construct it and call it in the same order. Tensors: fp16, contiguous, at most
+    ``max_elems`` elements, a multiple of 8. The sum runs in fp32 over ranks in rank order and is
+    rounded once. ``close()`` (collective) releases the regions.
+    """
+
+    def __init__(self, group=None, max_elems: int = 1 << 16):
+        import ctypes
+
+        from . import _ext
+
+        self._ct = ctypes
+        lib = ctypes.CDLL(_ext.C_LIBRARY)
+        vp = ctypes.c_void_p
+        lib.ashqk_p2p_region_bytes.argtypes = [ctypes.c_int64, ctypes.POINTER(ctypes.c_size_t)]
+        lib.ashqk_p2p_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
+        lib.ashqk_p2p_free.argtypes = [vp]
+        lib.ashqk_p2p_export.argtypes = [vp, vp]
+        lib.ashqk_p2p_import.argtypes = [vp, ctypes.POINTER(vp)]
+        lib.ashqk_p2p_close.argtypes = [vp]
+        lib.ashqk_allreduce_f16_oneshot.argtypes = [vp, vp, ctypes.c_int64, vp, ctypes.c_int, ctypes.c_int,
+                                                    ctypes.c_int64, vp]
+        self._lib, self.group = lib, group
+        self.rank, self.world = _world(group)
+        self.max_elems = int(max_elems)
+        size = ctypes.c_size_t(0)
+        if lib.ashqk_p2p_region_bytes(self.max_elems, ctypes.byref(size)) != 0:
+            raise ValueError("max_elems must be a positive multiple of 8")
+        region = vp()
+        if lib.ashqk_p2p_alloc(size.value, ctypes.byref(region)) != 0:
+            raise RuntimeError("ashqk: cannot allocate the all-reduce region")
+        self._region = region
+        handle = ctypes.create_string_buffer(64)
+        if lib.ashqk_p2p_export(region, handle) != 0:
+            raise RuntimeError("ashqk: cannot export the all-reduce region")
+        handles = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(handles, handle.raw, group=group)
+        else:
+            handles = [handle.raw]
+        self._imported = []
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(region.value)
+                continue
+            p = vp()
+            if lib.ashqk_p2p_import(ctypes.create_string_buffer(h, 64), ctypes.byref(p)) != 0:
+                raise RuntimeError(f"ashqk: cannot open rank {r}'s all-reduce region")
+            self._imported.append(p)
+            ptrs.append(p.value)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self._regions_dev = torch.tensor(ptrs, dtype=torch.int64, device=dev)
+        if self.world > 1:
+            dist.barrier(group=group)
+
+    def __call__(self, t: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Return the sum over ranks of ``t`` (in place when ``out is t``)."""
+        assert t.dtype == torch.float16 and t.is_cuda and t.is_contiguous(), "fp16 contiguous CUDA tensor"
+        assert t.numel() % 8 == 0 and t.numel() <= self.max_elems, "numel: a multiple of 8, <= max_elems"
+        out = torch.empty_like(t) if out is None else out
+        rc = self._lib.ashqk_allreduce_f16_oneshot(t.data_ptr(), out.data_ptr(), t.numel(),
+                                                   self._regions_dev.data_ptr(), self.rank, self.world,
+                                                   self.max_elems, torch.cuda.current_stream().cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"ashqk_allreduce_f16_oneshot failed ({rc})")
+        return out
+
+    def close(self) -> None:
+        """Collective: wait for every rank, then release the peer mappings and the region."""
+        if self._region is None:
+            return
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for p in self._imported:
+            self._lib.ashqk_p2p_close(p)
+        self._lib.ashqk_p2p_free(self._region)
+        self._region, self._imported = None, []

@@ -20,6 +20,7 @@ namespace ashqk {
 enum DeviceError : unsigned int {
   kDevErrTimeout = 1u,       // a pipeline wait ran past its limit
   kDevErrBadLaunch = 2u,     // kernel found launch parameters it cannot handle
+  kDevErrPeer = 4u,          // a peer rank never arrived at an all-reduce (sticky: later calls do nothing)
 };
 extern __device__ unsigned int g_device_errors;
 

@@ -134,6 +134,7 @@ def workload_config(world, n_layers=N_LAYERS):
         "model": "qwen3-8b linear layers (random AWQ weights)",
         "global_batch": 1, "seq_len": 1,
         "parallelism": f"tp{world}" if world > 1 else "none",
+        "tp_allreduce": os.environ.get("ASHQK_TP_ALLREDUCE", "nccl") if world > 1 else None,
         "l2": "inputs larger than L2: 3.6 GB of distinct per-layer weights per step",
     }
     if n_layers != N_LAYERS:  # a reduced stack (profiling runs), not the benchmark workload
@@ -237,11 +238,19 @@ def make_stack(world, rank, device, n_layers=N_LAYERS):
     return stack
 
 
-def stack_step(stack, h, world, group):
-    """One token through every linear layer (public API calls)."""
+def stack_step(stack, h, world, group, allreduce=None):
+    """One token through every linear layer (public API calls). The row-parallel partials are summed
+    with NCCL, or with ``allreduce`` (an ``ashqk.tp.P2PAllReduce``) when given."""
     import torch.distributed as dist
 
     from ashqk import w4a16_linear
+
+    def reduce(t):
+        if world > 1:
+            if allreduce is not None:
+                allreduce(t, out=t)
+            else:
+                dist.all_reduce(t, group=group)
 
     out = None
     for layer in stack:
@@ -249,13 +258,11 @@ def stack_step(stack, h, world, group):
         # Attention output stands in as the first columns of qkv (o input: 4096/P per rank).
         o_in = a[:, : 4096 // world]
         b = w4a16_linear(o_in, *layer["o"])                     # partial [M, 4096]
-        if world > 1:
-            dist.all_reduce(b, group=group)
+        reduce(b)
         c = w4a16_linear(b, *layer["gate_up"])                  # [M, 24576/P]
         d_in = c[:, : 12288 // world]
         out = w4a16_linear(d_in, *layer["down"])                # partial [M, 4096]
-        if world > 1:
-            dist.all_reduce(out, group=group)
+        reduce(out)
     return out
 
 
@@ -586,15 +593,22 @@ def run_gpu(args):
             print(json.dumps({"prefill": res}), flush=True)
         return
     stack = make_stack(world, rank, device, args.layers)
+    # Tensor-parallel reductions: NCCL by default, the NVLink one-shot kernel with
+    # ASHQK_TP_ALLREDUCE=p2p.
+    p2p = None
+    if world > 1 and os.environ.get("ASHQK_TP_ALLREDUCE", "nccl") == "p2p":
+        from ashqk import tp
+
+        p2p = tp.P2PAllReduce(group=group, max_elems=4 * 4096)
     results = {}
     graphs = {}
     for m in (1, 4):
         h = torch.randn(m, 4096, device=device).half()
-        stack_step(stack, h, world, group)  # warm-up outside capture (workspaces, NCCL comms)
+        stack_step(stack, h, world, group, p2p)  # warm-up outside capture (workspaces, NCCL comms)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            out = stack_step(stack, h, world, group)
+            out = stack_step(stack, h, world, group, p2p)
         graphs[m] = (g, h, out)
         del g  # the dict holds the only reference (graphs with NCCL calls must be freed before teardown)
 
@@ -643,6 +657,8 @@ def run_gpu(args):
     del g1, h1, out1
     graphs.clear()
     torch.cuda.synchronize()
+    if p2p is not None:
+        p2p.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

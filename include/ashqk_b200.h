@@ -127,7 +127,8 @@ ASHQK_API int ashqk_set_gemm_kernel(int which);
  * device after synchronising it. Bit 1: a pipeline wait inside a kernel ran
  * past its time limit and the kernel gave up (its output and any split-K
  * workspace it used are then invalid; re-zero the workspace). Bit 2: a kernel
- * rejected its launch parameters. No reference counterpart.
+ * rejected its launch parameters. Bit 3: a peer rank never arrived at
+ * ashqk_allreduce_f16_oneshot. No reference counterpart.
  */
 ASHQK_API int ashqk_get_device_errors(unsigned int* bits, int clear);
 
@@ -181,6 +182,32 @@ ASHQK_API int ashqk_dequantize_awq_f16(const int32_t* qweight, int64_t qw_ld, co
 ASHQK_API int ashqk_dequantize_awq_f32(const int32_t* qweight, int64_t qw_ld, const int32_t* qzeros,
                              int64_t qz_ld, const void* scales, int64_t s_ld, float* w, int64_t w_ld,
                              int N, int K, int group_size, void* stream);
+
+/*
+ * One-shot all-reduce of fp16 tensors over NVLink peer memory, for the
+ * tensor-parallel decode path (row-parallel partials of 8-128 KB, where NCCL's
+ * per-call cost dominates). No reference counterpart: the reference has no
+ * multi-GPU code. Usage, per rank (one process per GPU, same order everywhere):
+ * size a region for the largest tensor (ashqk_p2p_region_bytes), allocate it
+ * (ashqk_p2p_alloc, zeroed), exchange ashqk_p2p_export handles (64 bytes) with
+ * the peers, open theirs (ashqk_p2p_import), put the world's region pointers
+ * (own one at index rank) in a device array, and call
+ * ashqk_allreduce_f16_oneshot. Every rank must make the same sequence of calls;
+ * a rank that does not arrive within ~2 s makes the others give up (device
+ * error bit 3, output not written) rather than hang, and while that bit is set
+ * every later call returns at once; the regions are unusable after it.
+ * n: a multiple of 8 elements, <= max_elems;
+ * in/out 16-byte aligned (in == out allowed). Sum in fp32 over ranks in rank
+ * order, one rounding to fp16.
+ */
+ASHQK_API int ashqk_p2p_region_bytes(int64_t max_elems, size_t* bytes);
+ASHQK_API int ashqk_p2p_alloc(size_t bytes, void** ptr);
+ASHQK_API int ashqk_p2p_free(void* ptr);
+ASHQK_API int ashqk_p2p_export(void* ptr, void* handle64);
+ASHQK_API int ashqk_p2p_import(const void* handle64, void** ptr);
+ASHQK_API int ashqk_p2p_close(void* ptr);
+ASHQK_API int ashqk_allreduce_f16_oneshot(const void* in, void* out, int64_t n, const void* regions_dev, int rank,
+                                          int world, int64_t max_elems, void* stream);
 
 #ifdef __cplusplus
 }

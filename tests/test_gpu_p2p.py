@@ -1,0 +1,145 @@
+"""One-shot NVLink all-reduce kernel (``ashqk_allreduce_f16_oneshot``) on ONE GPU, with the host
+playing the peer rank: the peer's region is a second local buffer whose slot and flag the test
+writes before the call, so no kernel ever waits on another kernel. Checks the epoch/slot protocol,
+the fp32 rank-order sum, what the kernel publishes to the peer, and the bounded wait: a flag that
+nothing sets makes the kernel give up after about 2 s with the peer bit in the device error word,
+and later calls return at once until the bit is cleared. The real multi-GPU exchange is covered by
+``test_gpu_tp.py::test_p2p_allreduce``."""
+
+from __future__ import annotations
+
+import ctypes
+import time
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+HEADER = 256
+PEER_BIT = 4
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    from ashqk import _ext
+
+    lib = ctypes.CDLL(_ext.C_LIBRARY)
+    vp = ctypes.c_void_p
+    lib.ashqk_p2p_region_bytes.argtypes = [ctypes.c_int64, ctypes.POINTER(ctypes.c_size_t)]
+    lib.ashqk_allreduce_f16_oneshot.argtypes = [vp, vp, ctypes.c_int64, vp, ctypes.c_int, ctypes.c_int,
+                                                ctypes.c_int64, vp]
+    lib.ashqk_get_device_errors.argtypes = [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]
+    lib.ashqk_p2p_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
+    lib.ashqk_p2p_free.argtypes = [vp]
+    return lib
+
+
+def _errors(lib, clear=False):
+    bits = ctypes.c_uint(0)
+    assert lib.ashqk_get_device_errors(ctypes.byref(bits), int(clear)) == 0
+    return bits.value
+
+
+class _TwoRegions:
+    """Rank 0's region and the host-played rank 1's region, both on this GPU."""
+
+    def __init__(self, lib, max_elems):
+        size = ctypes.c_size_t(0)
+        assert lib.ashqk_p2p_region_bytes(max_elems, ctypes.byref(size)) == 0
+        self.max_elems, self.size = max_elems, size.value
+        self.slot_bytes = (self.size - HEADER) // 2
+        self.r = [torch.zeros(self.size, dtype=torch.uint8, device="cuda") for _ in range(2)]
+        self.ptrs = torch.tensor([t.data_ptr() for t in self.r], dtype=torch.int64, device="cuda")
+
+    def flags(self, q):
+        return self.r[q][64:96].view(torch.int32)
+
+    def epoch(self, q):
+        return int(self.r[q][0:4].view(torch.int32)[0])
+
+    def slot(self, q, parity, n):
+        off = HEADER + parity * self.slot_bytes
+        return self.r[q][off:off + 2 * n].view(torch.float16)
+
+
+def _call(lib, regs, x, out, rank=0, world=2):
+    return lib.ashqk_allreduce_f16_oneshot(x.data_ptr(), out.data_ptr(), x.numel(), regs.ptrs.data_ptr(), rank,
+                                           world, regs.max_elems, torch.cuda.current_stream().cuda_stream)
+
+
+def test_protocol_and_sum(lib):
+    assert _errors(lib, clear=True) & PEER_BIT == 0
+    regs = _TwoRegions(lib, 1 << 14)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    for epoch, shape in enumerate([(4, 4096), (1, 4096), (16, 1024), (2, 8)], start=1):
+        n = shape[0] * shape[1]
+        a = (torch.randn(shape, device="cuda", generator=g) * 2).half()
+        b = (torch.randn(shape, device="cuda", generator=g) * 2).half()
+        regs.slot(1, epoch & 1, n).copy_(b.view(-1))      # the peer's partial ...
+        regs.flags(0)[1] = epoch                           # ... and its arrival
+        out = torch.full_like(a, float("nan"))
+        assert _call(lib, regs, a, out) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(out, (a.float() + b.float()).half()), epoch
+        assert regs.epoch(0) == epoch
+        assert int(regs.flags(1)[0]) == epoch             # published to the peer
+        assert torch.equal(regs.slot(0, epoch & 1, n), a.view(-1))
+    # in place, world = 1 (no peers, a copy through the slot)
+    a = torch.randn(8, 512, device="cuda", generator=g).half()
+    ref = a.clone()
+    assert _call(lib, regs, a, a, world=1) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(a, ref)
+    assert _errors(lib) & PEER_BIT == 0
+
+
+def test_rejects_bad_arguments(lib):
+    regs = _TwoRegions(lib, 1024)
+    a = torch.zeros(1024, dtype=torch.float16, device="cuda")
+    out = torch.empty_like(a)
+    bad = [
+        dict(x=a[:12], out=out[:12]),                     # not a multiple of 8
+        dict(x=a[1:9], out=out[:8]),                       # misaligned input
+        dict(x=torch.zeros(2048, dtype=torch.float16, device="cuda"), out=torch.empty(2048, dtype=torch.float16,
+                                                                                    device="cuda")),  # > max
+        dict(x=a, out=out, rank=2),                        # rank outside world
+        dict(x=a, out=out, world=9),                       # more ranks than supported
+    ]
+    for kw in bad:
+        assert _call(lib, regs, **kw) == 1, kw
+    p = ctypes.c_void_p()
+    assert lib.ashqk_p2p_alloc(4096, ctypes.byref(p)) == 0 and p.value
+    assert lib.ashqk_p2p_free(p) == 0
+
+
+def test_missing_peer_times_out(lib):
+    regs = _TwoRegions(lib, 1024)
+    a = torch.ones(1024, dtype=torch.float16, device="cuda")
+    out = torch.full_like(a, -7.0)
+    _errors(lib, clear=True)
+    t0 = time.time()
+    assert _call(lib, regs, a, out) == 0                   # nothing ever sets the peer's flag
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    try:
+        assert _errors(lib) & PEER_BIT
+        assert 0.5 < waited < 30, waited
+        assert bool((out == -7.0).all())                   # output left unwritten
+        # sticky: the next call returns at once and does nothing
+        regs.flags(0)[1] = 2
+        t0 = time.time()
+        assert _call(lib, regs, a, out) == 0
+        torch.cuda.synchronize()
+        assert time.time() - t0 < 0.5
+        assert regs.epoch(0) == 1 and bool((out == -7.0).all())
+    finally:
+        _errors(lib, clear=True)
+    # cleared: the kernel runs again (the peer's flag now covers epoch 2)
+    regs.slot(1, 0, 1024).fill_(3.0)
+    assert _call(lib, regs, a, out) == 0
+    torch.cuda.synchronize()
+    assert bool((out == 4.0).all()) and _errors(lib) == 0

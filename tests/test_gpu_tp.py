@@ -148,3 +148,73 @@ def test_tp_mlp_rank_shapes(layer, m, world):
     e_cublas = float(((x @ w32.half()).float() - y_true).norm() / y_true.norm())
     e = float((y.float() - y_true).norm() / y_true.norm())
     assert e <= 2 * e_cublas + 1e-5, (e, e_cublas)
+
+
+def _p2p_worker(rank, world, port):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        from ashqk import tp
+
+        ar = tp.P2PAllReduce(max_elems=1 << 16)
+
+        def data(trial, r, shape=(4, 4096)):
+            g = torch.Generator(device=dev)
+            g.manual_seed(1000 * trial + r)
+            return (torch.randn(shape, device=dev, generator=g) * 0.5).half()
+
+        def expected(trial, shape=(4, 4096)):
+            acc = torch.zeros(shape, dtype=torch.float32, device=dev)
+            for r in range(world):  # rank order, fp32, one rounding: the kernel's definition
+                acc += data(trial, r, shape).float()
+            return acc.half()
+
+        for trial in range(6):  # consecutive epochs alternate the two slots
+            shape = (1, 4096) if trial % 2 else (16, 4096)
+            y = ar(data(trial, rank, shape))
+            assert torch.equal(y, expected(trial, shape)), trial
+        t = data(7, rank)
+        ar(t, out=t)  # in place
+        assert torch.equal(t, expected(7))
+        static = data(8, rank)
+        out = torch.empty_like(static)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            ar(static, out=out)
+        for trial in (9, 10, 11):
+            static.copy_(data(trial, rank))
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out, expected(trial)), trial
+        del graph
+        # against NCCL on a row-parallel layer
+        n, k = 4096, 4096
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(5)
+        qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (k, n // 8), dtype=torch.int32, device=dev, generator=gen)
+        qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (k // 128, n // 8), dtype=torch.int32, device=dev, generator=gen)
+        s = (torch.rand((k // 128, n), device=dev, generator=gen) * 0.018 + 0.002).half()
+        x = torch.randn(2, k, device=dev, generator=gen).half()
+        xs, sh = tp.shard_input(x, rank, world), tp.shard_rows(qw, qz, s, rank, world)
+        y_p2p = tp.row_parallel_linear(xs, *sh, allreduce=ar)
+        y_nccl = tp.row_parallel_linear(xs, *sh, reduce_dtype=torch.float32)
+        assert float((y_p2p.float() - y_nccl.float()).abs().max()) <= 1e-2 * float(y_nccl.float().abs().max())
+        ar.close()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2+ GPUs")
+def test_p2p_allreduce():
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 8)
+    mp.start_processes(_p2p_worker, args=(world, _free_port()), nprocs=world, start_method="spawn", join=True)
