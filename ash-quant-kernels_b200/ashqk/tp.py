@@ -199,6 +199,7 @@ class P2PAllReduce:
         lib.ashqk_p2p_export.argtypes = [vp, vp]
         lib.ashqk_p2p_import.argtypes = [vp, ctypes.POINTER(vp)]
         lib.ashqk_p2p_close.argtypes = [vp]
+        lib.ashqk_get_device_errors.argtypes = [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]
         lib.ashqk_allreduce_f16_oneshot.argtypes = [vp, vp, ctypes.c_int64, vp, ctypes.c_int, ctypes.c_int,
                                                     ctypes.c_int64, vp]
         self._lib, self.group = lib, group
@@ -246,6 +247,14 @@ class P2PAllReduce:
         if rc != 0:
             raise RuntimeError(f"ashqk_allreduce_f16_oneshot failed ({rc})")
         return out
+
+    def check(self) -> None:
+        """Raise if a call on this device gave up waiting for a peer (the results since are invalid)."""
+        bits = self._ct.c_uint(0)
+        if self._lib.ashqk_get_device_errors(self._ct.byref(bits), 0) != 0:
+            raise RuntimeError("ashqk: cannot read the device error word")
+        if bits.value & 4:
+            raise RuntimeError("ashqk: a peer rank never arrived at a P2P all-reduce; its results are invalid")
 
     def close(self) -> None:
         """Collective: wait for every rank, then release the peer mappings and the region."""

@@ -658,6 +658,7 @@ def run_gpu(args):
     graphs.clear()
     torch.cuda.synchronize()
     if p2p is not None:
+        p2p.check()  # a timed-out peer wait would have made the timed calls no-ops
         p2p.close()
     if world > 1:
         dist.barrier()

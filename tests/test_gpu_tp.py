@@ -206,6 +206,7 @@ def _p2p_worker(rank, world, port):
         y_p2p = tp.row_parallel_linear(xs, *sh, allreduce=ar)
         y_nccl = tp.row_parallel_linear(xs, *sh, reduce_dtype=torch.float32)
         assert float((y_p2p.float() - y_nccl.float()).abs().max()) <= 1e-2 * float(y_nccl.float().abs().max())
+        ar.check()
         ar.close()
         dist.barrier()
     finally:
