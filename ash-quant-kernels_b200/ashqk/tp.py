@@ -185,13 +185,15 @@ class P2PAllReduce:
     rounded once. ``close()`` (collective) releases the regions.
     """
 
-    def __init__(self, group=None, max_elems: int = 1 << 16):
+    def __init__(self, group=None, max_elems: int = 1 << 16, lib=None):
+        """``lib``: the loaded C library (default: the package's own; tests pass a fake)."""
         import ctypes
 
-        from . import _ext
-
         self._ct = ctypes
-        lib = ctypes.CDLL(_ext.C_LIBRARY)
+        if lib is None:
+            from . import _ext
+
+            lib = ctypes.CDLL(_ext.C_LIBRARY)
         vp = ctypes.c_void_p
         lib.ashqk_p2p_region_bytes.argtypes = [ctypes.c_int64, ctypes.POINTER(ctypes.c_size_t)]
         lib.ashqk_p2p_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
@@ -211,36 +213,59 @@ class P2PAllReduce:
         region = vp()
         if lib.ashqk_p2p_alloc(size.value, ctypes.byref(region)) != 0:
             raise RuntimeError("ashqk: cannot allocate the all-reduce region")
-        self._region = region
+        self._region, self._imported = region, []
         handle = ctypes.create_string_buffer(64)
-        if lib.ashqk_p2p_export(region, handle) != 0:
-            raise RuntimeError("ashqk: cannot export the all-reduce region")
+        # Every rank takes part in the handle exchange even when its own export
+        # failed (an empty handle), so that a local failure raises on every rank
+        # instead of leaving the peers waiting in the collective.
+        ok = lib.ashqk_p2p_export(region, handle) == 0
         handles = [None] * self.world
         if self.world > 1:
-            dist.all_gather_object(handles, handle.raw, group=group)
+            dist.all_gather_object(handles, handle.raw if ok else b"", group=group)
         else:
             handles = [handle.raw]
-        self._imported = []
-        ptrs = []
-        for r, h in enumerate(handles):
-            if r == self.rank:
-                ptrs.append(region.value)
-                continue
-            p = vp()
-            if lib.ashqk_p2p_import(ctypes.create_string_buffer(h, 64), ctypes.byref(p)) != 0:
-                raise RuntimeError(f"ashqk: cannot open rank {r}'s all-reduce region")
-            self._imported.append(p)
-            ptrs.append(p.value)
-        dev = torch.device("cuda", torch.cuda.current_device())
-        self._regions_dev = torch.tensor(ptrs, dtype=torch.int64, device=dev)
+        err, ptrs = None, []
+        bad = [r for r, h in enumerate(handles) if len(h) != 64]
+        if bad:
+            err = f"ranks {bad} could not export their regions"
+        else:
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(region.value)
+                    continue
+                p = vp()
+                if lib.ashqk_p2p_import(ctypes.create_string_buffer(h, 64), ctypes.byref(p)) != 0:
+                    err = f"cannot open rank {r}'s region"
+                    break
+                self._imported.append(p)
+                ptrs.append(p.value)
+        # Agree on the outcome (this exchange is also the barrier after which
+        # every region is open), so that all ranks raise together or none does.
+        errors = [err] * self.world
         if self.world > 1:
-            dist.barrier(group=group)
+            dist.all_gather_object(errors, err, group=group)
+        failed = [f"rank {r}: {e}" for r, e in enumerate(errors) if e]
+        try:
+            if failed:
+                raise RuntimeError("ashqk: P2P all-reduce setup failed (" + "; ".join(failed) + ")")
+            dev = torch.device("cuda", torch.cuda.current_device())
+            self._regions_dev = torch.tensor(ptrs, dtype=torch.int64, device=dev)
+        except BaseException:
+            for p in self._imported:
+                lib.ashqk_p2p_close(p)
+            lib.ashqk_p2p_free(region)
+            self._region, self._imported = None, []
+            raise
 
     def __call__(self, t: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Return the sum over ranks of ``t`` (in place when ``out is t``)."""
         assert t.dtype == torch.float16 and t.is_cuda and t.is_contiguous(), "fp16 contiguous CUDA tensor"
         assert t.numel() % 8 == 0 and t.numel() <= self.max_elems, "numel: a multiple of 8, <= max_elems"
-        out = torch.empty_like(t) if out is None else out
+        assert self._region is not None, "P2PAllReduce is closed"
+        if out is None:
+            out = torch.empty_like(t)
+        assert (out.dtype == torch.float16 and out.device == t.device and out.is_contiguous()
+                and out.numel() == t.numel()), "out: fp16, contiguous, same device and size as t"
         rc = self._lib.ashqk_allreduce_f16_oneshot(t.data_ptr(), out.data_ptr(), t.numel(),
                                                    self._regions_dev.data_ptr(), self.rank, self.world,
                                                    self.max_elems, torch.cuda.current_stream().cuda_stream)

@@ -37,6 +37,53 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+class _FakeP2PLib:
+    """Stands in for the C library's P2P entry points on CPU: records every call and fails the
+    one named by ``fail`` on this rank."""
+
+    def __init__(self, rank, fail=None):
+        self.calls, self.open, self.freed = [], [], []
+
+        def region_bytes(n, size_ref):
+            size_ref._obj.value = 256 + 4 * n
+            return 0
+
+        def alloc(nbytes, ptr_ref):
+            ptr_ref._obj.value = 0x1000 * (rank + 1)
+            return 0
+
+        def export(ptr, handle):
+            self.calls.append("export")
+            if fail == "export":
+                return 5
+            handle.raw = bytes([rank]) * 64
+            return 0
+
+        def import_(handle, ptr_ref):
+            self.calls.append("import")
+            if fail == "import":
+                return 5
+            ptr_ref._obj.value = 0x100000 + handle.raw[0]
+            self.open.append(ptr_ref._obj.value)
+            return 0
+
+        def close(ptr):
+            self.open.remove(ptr.value if hasattr(ptr, "value") else ptr)
+            return 0
+
+        def free(ptr):
+            self.freed.append(ptr.value if hasattr(ptr, "value") else ptr)
+            return 0
+
+        def nop(*args):
+            return 0
+
+        self.ashqk_p2p_region_bytes, self.ashqk_p2p_alloc, self.ashqk_p2p_export = region_bytes, alloc, export
+        self.ashqk_p2p_import, self.ashqk_p2p_close, self.ashqk_p2p_free = import_, close, free
+        self.ashqk_allreduce_f16_oneshot = nop
+        self.ashqk_get_device_errors = nop
+
+
 def _worker(rank, port, case):
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
     dist.init_process_group("gloo", rank=rank, world_size=WORLD)
@@ -89,6 +136,18 @@ def _worker(rank, port, case):
             others = [torch.empty_like(y) for _ in range(WORLD)]
             dist.all_gather(others, y)
             assert all(torch.equal(o, y) for o in others)
+        elif case.startswith("p2p_"):
+            # A failed setup step on one rank makes every rank raise (no rank is left waiting in a
+            # collective), and each releases what it had opened and allocated. On CPU even a clean
+            # exchange fails at the end (no CUDA device for the pointer table): the same cleanup.
+            what, where = {"p2p_export": ("export", 1), "p2p_import": ("import", 0), "p2p_ok": (None, -1)}[case]
+            lib = _FakeP2PLib(rank, what if rank == where else None)
+            with pytest.raises(RuntimeError) as info:
+                tp.P2PAllReduce(max_elems=1024, lib=lib)
+            if what is not None:
+                assert f"rank {where}:" in str(info.value), str(info.value)
+            assert lib.open == [] and lib.freed == [0x1000 * (rank + 1)]
+            assert lib.calls.count("import") == (0 if what == "export" else 1)
         elif case == "bad_split":
             qw = torch.zeros(384, 8, dtype=torch.int32)  # K=384, G=128: 3 groups
             qz = torch.zeros(3, 8, dtype=torch.int32)
@@ -102,7 +161,7 @@ def _worker(rank, port, case):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("case", ["column", "row", "mlp", "bad_split"])
+@pytest.mark.parametrize("case", ["column", "row", "mlp", "bad_split", "p2p_export", "p2p_import", "p2p_ok"])
 def test_tensor_parallel_gloo(case):
     mp.start_processes(_worker, args=(_free_port(), case), nprocs=WORLD, start_method="spawn", join=True)
 
