@@ -507,3 +507,27 @@ int gemv_strip_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t 
 }
 
 }  // namespace ashqk
+
+extern "C" int ashqk_gemv_strip_plan(int M, int N, int K, int group_size, int sm_count, ashqk_strip_plan* plan) {
+  if (!plan || M <= 0 || N <= 0 || K <= 0 || group_size <= 0 || N % 8 || K % group_size || sm_count < 0)
+    return ASHQK_ERR_INVALID_ARGUMENT;
+  if (M > 16 || N % 32 || group_size % 16) return ASHQK_ERR_UNSUPPORTED;
+  if (sm_count == 0) {
+    ashqk::DeviceInfo info;
+    const int rc = ashqk::device_info(&info);
+    if (rc) return rc;
+    sm_count = info.sm_count;
+  }
+  ashqk::StripPlan p;
+  if (!ashqk::plan_strip(M, N, K, group_size, sm_count, &p)) return ASHQK_ERR_UNSUPPORTED;
+  plan->grid_x = p.tiles;
+  plan->grid_y = p.ksplit;
+  // The launch instantiates 4 or 8 consumer warps when M > 8 (16 is planned only for M <= 8).
+  plan->consumer_warps = p.consumers;
+  plan->threads = 32 * (p.consumers + 1);
+  plan->ring_stages = p.ring;
+  plan->stages_total = p.stages_total;
+  plan->stage_bytes = p.stage_bytes;
+  plan->smem_bytes = static_cast<int>(p.smem);
+  return ASHQK_OK;
+}

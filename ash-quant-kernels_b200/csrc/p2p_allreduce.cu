@@ -53,6 +53,10 @@ __global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(const __hal
   __shared__ unsigned int epoch_s;
   __shared__ int failed_s;
   unsigned char* mine = regions[rank];
+  // The next kernel (the next layer's GEMV) may launch now and stream its
+  // weights while this one waits for the peers; it reads our output only after
+  // its own griddepcontrol.wait, i.e. after this grid has completed.
+  pdl_launch_dependents();
   pdl_wait();  // the partial is the previous kernel's output
   if (threadIdx.x == 0) {
     failed_s = (atomicOr(&g_device_errors, 0u) & kDevErrPeer) != 0;

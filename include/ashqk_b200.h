@@ -184,6 +184,27 @@ ASHQK_API int ashqk_dequantize_awq_f32(const int32_t* qweight, int64_t qw_ld, co
                              int N, int K, int group_size, void* stream);
 
 /*
+ * Launch plan of the column-strip decode GEMV (the default kernel for M <= 16
+ * on 16-byte aligned operands) for an M x N x K problem with the given group
+ * size on sm_count SMs (0: the current device's). Host arithmetic only: with
+ * sm_count > 0 it needs no GPU. The counterpart of the reference's launch
+ * configuration choice, _default_config (ashqk/kernels/w4a16_gemv.py:123-129).
+ * Returns ASHQK_ERR_UNSUPPORTED for problems the strip kernel does not take
+ * (M > 16, N % 32, group_size % 16).
+ */
+typedef struct {
+  int grid_x;          /* column strips of 64 outputs */
+  int grid_y;          /* CTAs sharing a strip's K range (one cluster along y when > 1) */
+  int threads;         /* per CTA: one producer warp + the consumer warps */
+  int consumer_warps;  /* 4, 8 or 16 */
+  int ring_stages;     /* 256-row stages resident in shared memory */
+  int stages_total;    /* ceil(K / 256) */
+  int stage_bytes;     /* bytes of one stage: weights, x, scale and zero rows */
+  int smem_bytes;      /* dynamic shared memory per CTA */
+} ashqk_strip_plan;
+ASHQK_API int ashqk_gemv_strip_plan(int M, int N, int K, int group_size, int sm_count, ashqk_strip_plan* plan);
+
+/*
  * One-shot all-reduce of fp16 tensors over NVLink peer memory, for the
  * tensor-parallel decode path (row-parallel partials of 8-128 KB, where NCCL's
  * per-call cost dominates). No reference counterpart: the reference has no

@@ -91,3 +91,72 @@ def test_workspace_size_queries(lib):
     if not torch.cuda.is_available():
         assert lib.ashqk_gemm_workspace_size(2048, 24576, 4096, 128, ctypes.byref(sz)) == 5
         assert lib.ashqk_gemv_workspace_size(1, 6144, 4096, 128, 0, ctypes.byref(sz)) == 5
+
+
+class StripPlan(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_int) for name in ("grid_x", "grid_y", "threads", "consumer_warps", "ring_stages",
+                                                 "stages_total", "stage_bytes", "smem_bytes")]
+
+
+def _strip_plan(lib, m, n, k, g, sms):
+    lib.ashqk_gemv_strip_plan.argtypes = [ctypes.c_int] * 5 + [ctypes.POINTER(StripPlan)]
+    p = StripPlan()
+    return lib.ashqk_gemv_strip_plan(m, n, k, g, sms, ctypes.byref(p)), p
+
+
+# Qwen3-8B decode layers, the config-5 TP shards, Qwen3.5 skinny layers, and small / ragged ones.
+_SHAPES = [(6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288), (57344 // 8, 8192), (8192, 28672 // 8),
+           (64, 4096), (96, 4096), (160, 256), (32, 128), (4096, 128), (28672, 8192)]
+
+
+@pytest.mark.parametrize("sms", [148, 132, 8])
+def test_strip_plan_invariants(lib, sms):
+    """The column-strip GEMV's launch plan, over decode shapes and every M it takes: the shared
+    memory fits one CTA of an SM (225 KB dynamic), every CTA of the grid is resident at once
+    (unless even one-stage rings cannot make that so, which only an 8-SM part reaches),
+    ring slots hold whole stages, the warp count matches a compiled variant, and a K split is a
+    cluster of at most 4 CTAs that each own at least one stage."""
+    for n, k in _SHAPES:
+        for g in (32, 64, 128):
+            if k % g:
+                continue
+            for m in range(1, 17):
+                rc, p = _strip_plan(lib, m, n, k, g, sms)
+                assert rc == 0, (m, n, k, g, rc)
+                where = (m, n, k, g, sms)
+                assert p.grid_x == -(-n // 64) and p.stages_total == -(-k // 256), where
+                assert 1 <= p.grid_y <= 4 and p.grid_y <= p.stages_total, where
+                assert p.consumer_warps in ((4, 8, 16) if m <= 8 else (4, 8)), where
+                assert p.threads == 32 * (p.consumer_warps + 1) <= 1024, where
+                assert 1 <= p.ring_stages <= 24, where
+                assert p.ring_stages <= -(-p.stages_total // p.grid_y), where  # no idle slot
+                assert p.stage_bytes % 128 == 0 and p.ring_stages * p.stage_bytes + 1024 <= p.smem_bytes, where
+                assert p.smem_bytes <= 225 * 1024, where
+                per_sm = -(-(p.grid_x * p.grid_y) // sms)
+                if p.ring_stages > 1:  # a one-stage ring is the floor; below it CTAs take turns
+                    assert per_sm * (p.smem_bytes + 1024) <= 228 * 1024, where
+                # more consumer warps than slots only at the 4-warp floor (the extra warps idle)
+                assert p.consumer_warps <= max(p.ring_stages, 4), where
+
+
+def test_strip_plan_rejects(lib):
+    assert _strip_plan(lib, 17, 4096, 4096, 128, 148)[0] == 2     # M > 16: the chunked path
+    assert _strip_plan(lib, 1, 4104, 4096, 128, 148)[0] == 2      # N % 32
+    assert _strip_plan(lib, 1, 4096, 4096, 8, 148)[0] == 2        # G % 16
+    assert _strip_plan(lib, 1, 4096, 4000, 128, 148)[0] == 1      # K % G
+    assert _strip_plan(lib, 0, 4096, 4096, 128, 148)[0] == 1
+    assert _strip_plan(lib, 1, 4096, 4096, 128, -1)[0] == 1
+    import torch
+
+    if not torch.cuda.is_available():
+        assert _strip_plan(lib, 1, 4096, 4096, 128, 0)[0] == 5      # SM count of a missing device
+
+
+def test_strip_plan_of_the_measured_layers(lib):
+    """At M=1 on 148 SMs the planner picks the launch shapes the committed strip-GEMV profile
+    measured for the Qwen3-8B layers (grid, cluster split, warps per CTA)."""
+    want = {(6144, 4096): (96, 1, 544), (4096, 4096): (64, 2, 288), (24576, 4096): (384, 1, 160),
+            (4096, 12288): (64, 4, 288)}
+    for (n, k), (gx, gy, threads) in want.items():
+        rc, p = _strip_plan(lib, 1, n, k, 128, 148)
+        assert rc == 0 and (p.grid_x, p.grid_y, p.threads) == (gx, gy, threads), (n, k, p.grid_x, p.grid_y, p.threads)
