@@ -119,7 +119,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": max(args.warmup, 1), "ms_per_step": round(value / 1e3, 3),
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (fp16 in/out)",
-        "data": "synthetic", "config": workload_config(1),
+        "data": "synthetic", "config": workload_config(args.gpus),  # the same workload keys as our arm
         "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
