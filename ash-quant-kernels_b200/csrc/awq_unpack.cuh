@@ -14,6 +14,9 @@
 namespace ashqk {
 
 constexpr uint32_t kSixteenthX2 = 0x2C002C00u;     // half2(1/16, 1/16)
+constexpr uint32_t kOneX2 = 0x3C003C00u;           // half2(1, 1)
+// Nibble of a packed AWQ word holding column c (inverse of AWQ_ORDER, ashqk/ref.py:20-22).
+__device__ constexpr int kAwqNibbleOfCol[8] = {0, 4, 1, 5, 2, 6, 3, 7};
 constexpr uint32_t kNegSixteenthX2 = 0xAC00AC00u;  // half2(-1/16, -1/16)
 
 // 1024+q (low nibble) or 1024+16q (high nibble) -> q - z, exact in fp16.
@@ -47,7 +50,8 @@ __device__ __forceinline__ void zero_consts(uint32_t zw, uint32_t (&zc)[8]) {
 
 // Magic-number halves without the zero-point subtraction: slots 0 and 2 hold
 // 1024 + q (low nibbles), slots 1 and 3 hold 1024 + 16 q (high nibbles). Dot
-// products of these with x are corrected once per group (see gemv_tma.cu).
+// products of these with x are corrected once per group (the RAW variant of
+// the column-strip GEMV).
 __device__ __forceinline__ void unpack_raw(uint32_t T, uint32_t (&o)[4]) {
   const uint32_t T8 = T >> 8;
   o[0] = lop3_and_or(T, kLoNibbles, kMagic1024x2);

@@ -63,7 +63,13 @@ struct StripMaps {
   CUtensorMap qw, x, s, z;
 };
 
-template <int MT, int C>
+// RAW: feed the magic-number halves (1024 + q, 1024 + 16 q) to the mma without
+// subtracting the zero point per weight, accumulate each group's sum of x with
+// one more mma against a fragment of ones, and correct once per group:
+// sum x (q - z) = f * dot - (c + z) * sum x, with f = 1, c = 1024 for the
+// low-nibble columns (0, 1, 4, 5 of a word) and f = 1/16, c = 64 for the
+// high-nibble ones (2, 3, 6, 7). 16 fewer instructions per 16-row step.
+template <int MT, int C, bool RAW>
 __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_constant__ StripMaps maps,
                                                                   const StripArgs a) {
   extern __shared__ unsigned char smem_raw[];
@@ -161,7 +167,13 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
       for (int j = 0; j < 4; ++j)
 #pragma unroll
         for (int r = 0; r < 4; ++r) part[mt][j][r] = 0.f;
-    uint32_t zc[8];
+    float psx[MT][4];  // RAW: the group's sum of x per token (c0: token 8mt+2t, c1: 8mt+2t+1)
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) psx[mt][r] = 0.f;
+    uint32_t zc[8];   // zero-point constants (subtracting variant)
+    float zk[8];      // RAW: c + z of columns 0..7 of word g
     uint32_t sh[4];
     int cur_grp = -1;
 
@@ -174,9 +186,17 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
         sc[2 * i + 1] = f.y;
       }
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
+      for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
+          if (RAW) {
+            // mma j holds column j (rows g) and j + 4 (rows g + 8) of word g.
+            const float f = j < 2 ? 1.f : 0.0625f;
+            part[mt][j][0] = fmaf(part[mt][j][0], f, -zk[j] * psx[mt][0]);
+            part[mt][j][1] = fmaf(part[mt][j][1], f, -zk[j] * psx[mt][1]);
+            part[mt][j][2] = fmaf(part[mt][j][2], f, -zk[4 + j] * psx[mt][0]);
+            part[mt][j][3] = fmaf(part[mt][j][3], f, -zk[4 + j] * psx[mt][1]);
+          }
           acc[mt][j][0] = fmaf(sc[j], part[mt][j][0], acc[mt][j][0]);
           acc[mt][j][1] = fmaf(sc[j], part[mt][j][1], acc[mt][j][1]);
           acc[mt][j][2] = fmaf(sc[4 + j], part[mt][j][2], acc[mt][j][2]);
@@ -184,6 +204,10 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
 #pragma unroll
           for (int r = 0; r < 4; ++r) part[mt][j][r] = 0.f;
         }
+        if (RAW)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) psx[mt][r] = 0.f;
+      }
     };
 
     int grp_end = -1;
@@ -205,7 +229,15 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
           const int grp = k / a.G;
           grp_end = (grp + 1) * a.G;
           const uint32_t gslot = static_cast<uint32_t>(grp - gbase);
-          zero_consts(lds_u32(base + a.z_off + gslot * (kStripWords * 4) + 4 * g), zc);
+          const uint32_t zw = lds_u32(base + a.z_off + gslot * (kStripWords * 4) + 4 * g);
+          if (RAW) {
+            // Column c of the word sits in nibble kAwqNibbleOfCol[c] (AWQ order).
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              zk[c] = static_cast<float>((zw >> (4 * kAwqNibbleOfCol[c])) & 15u) + ((c & 2) ? 64.f : 1024.f);
+          } else {
+            zero_consts(zw, zc);
+          }
           const uint4 sv = lds_v4(base + a.s_off + gslot * (kStripCols * 2) + 16 * g);
           sh[0] = sv.x;
           sh[1] = sv.y;
@@ -217,13 +249,20 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
         uint32_t w[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) w[q] = lds_u32(wrow + roff[q]);
-        const uint32_t za[4] = {zc[0], zc[1], zc[2], zc[3]};
-        const uint32_t zb[4] = {zc[4], zc[5], zc[6], zc[7]};
         uint32_t oa[4], ob[4], oc[4], od[4];
-        unpack_pairs(prmt(w[0], w[1], 0x6420u), za, oa);
-        unpack_pairs(prmt(w[0], w[1], 0x7531u), zb, ob);
-        unpack_pairs(prmt(w[2], w[3], 0x6420u), za, oc);
-        unpack_pairs(prmt(w[2], w[3], 0x7531u), zb, od);
+        if (RAW) {
+          unpack_raw(prmt(w[0], w[1], 0x6420u), oa);
+          unpack_raw(prmt(w[0], w[1], 0x7531u), ob);
+          unpack_raw(prmt(w[2], w[3], 0x6420u), oc);
+          unpack_raw(prmt(w[2], w[3], 0x7531u), od);
+        } else {
+          const uint32_t za[4] = {zc[0], zc[1], zc[2], zc[3]};
+          const uint32_t zb[4] = {zc[4], zc[5], zc[6], zc[7]};
+          unpack_pairs(prmt(w[0], w[1], 0x6420u), za, oa);
+          unpack_pairs(prmt(w[0], w[1], 0x7531u), zb, ob);
+          unpack_pairs(prmt(w[2], w[3], 0x6420u), za, oc);
+          unpack_pairs(prmt(w[2], w[3], 0x7531u), zb, od);
+        }
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
           uint32_t b0 = 0u, b1 = 0u;
@@ -237,6 +276,10 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
             const int sl = ((j & 1) << 1) | (j >> 1);
             const uint32_t A[4] = {oa[sl], ob[sl], oc[sl], od[sl]};
             mma_16816(part[mt][j], A, b0, b1);
+          }
+          if (RAW) {
+            const uint32_t ones[4] = {kOneX2, kOneX2, kOneX2, kOneX2};
+            mma_16816(psx[mt], ones, b0, b1);
           }
         }
       }
@@ -416,13 +459,13 @@ bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p) {
   return true;
 }
 
-template <int MT, int C>
-int launch_strip(const StripMaps& maps, const StripArgs& args, int tiles, size_t smem, cudaStream_t stream) {
+template <int MT, int C, bool RAW>
+int launch_strip_t(const StripMaps& maps, const StripArgs& args, int tiles, size_t smem, cudaStream_t stream) {
   const int ks = args.ksplit;
   static std::atomic<bool> configured[64];  // zero-initialised (static storage)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ASHQK_ERR_CUDA;
-  auto kernel = gemv_strip_kernel<MT, C>;
+  auto kernel = gemv_strip_kernel<MT, C, RAW>;
   if (!configured[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
@@ -453,6 +496,20 @@ int launch_strip(const StripMaps& maps, const StripArgs& args, int tiles, size_t
   cfg.numAttrs = n;
   if (cudaLaunchKernelEx(&cfg, kernel, maps, args) != cudaSuccess) return ASHQK_ERR_CUDA;
   return ASHQK_OK;
+}
+
+bool raw_unpack() {
+  static const bool on = [] {
+    const char* e = std::getenv("ASHQK_STRIP_RAW");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
+template <int MT, int C>
+int launch_strip(const StripMaps& maps, const StripArgs& args, int tiles, size_t smem, cudaStream_t stream) {
+  return raw_unpack() ? launch_strip_t<MT, C, true>(maps, args, tiles, smem, stream)
+                      : launch_strip_t<MT, C, false>(maps, args, tiles, smem, stream);
 }
 
 }  // namespace
