@@ -69,7 +69,16 @@ struct StripMaps {
 // sum x (q - z) = f * dot - (c + z) * sum x, with f = 1, c = 1024 for the
 // low-nibble columns (0, 1, 4, 5 of a word) and f = 1/16, c = 64 for the
 // high-nibble ones (2, 3, 6, 7). 16 fewer instructions per 16-row step.
-template <int MT, int C, bool RAW>
+//
+// PERM: permute k inside every 16-row step so that the four rows a lane reads
+// are t, t+4, t+8, t+12 (banks 8t..8t+7: conflict-free) instead of 2t, 2t+1,
+// 2t+8, 2t+9 (lanes t and t+2 share banks). Any k order gives the same dot
+// product as long as x follows it, so the warp owning a slot rewrites that
+// stage's x once before its steps: each 16-value block becomes
+// (x0, x4, x1, x5, x2, x6, x3, x7, x8, x12, ...), and token m's 16-byte chunk
+// c moves to chunk c ^ (m & 7) so that the 8 tokens of an mma fragment, 512
+// bytes apart, also read distinct banks.
+template <int MT, int C, bool RAW, bool PERM>
 __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_constant__ StripMaps maps,
                                                                   const StripArgs a) {
   extern __shared__ unsigned char smem_raw[];
@@ -152,7 +161,8 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
     // Row offsets (bytes) of rows {2t, 2t+1, 2t+8, 2t+9} of step 0, word g.
     uint32_t roff[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) roff[q] = (2 * t + (q & 1) + 8 * (q >> 1)) * (kStripWords * 4) + 4 * g;
+    for (int q = 0; q < 4; ++q)
+      roff[q] = (PERM ? t + 4 * q : 2 * t + (q & 1) + 8 * (q >> 1)) * (kStripWords * 4) + 4 * g;
     bool xok[MT];
     uint32_t xrow[MT];
 #pragma unroll
@@ -218,6 +228,23 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
       const int slot = li - round;  // round = the first stage of this pass over the ring
       if (!mbar_wait(&full[slot], (li / a.ring) & 1, &abort_flag)) break;
       const uint32_t base = smem_s + slot * a.stage_bytes;
+      if (PERM) {
+        // Rewrite this stage's x in the permuted, chunk-rotated order (row m:
+        // 32 chunks of 8 halves; lane l takes chunk l).
+        const uint32_t xb = base + a.x_off;
+        for (int m = 0; m < a.M; ++m) {
+          const uint4 v = lds_v4(xb + m * kXRowBytes + lane * 16);
+          uint4 o;
+          o.x = prmt(v.x, v.z, 0x5410u);  // (x0, x4)
+          o.y = prmt(v.x, v.z, 0x7632u);  // (x1, x5)
+          o.z = prmt(v.y, v.w, 0x5410u);  // (x2, x6)
+          o.w = prmt(v.y, v.w, 0x7632u);  // (x3, x7)
+          __syncwarp();  // every lane has read row m before any lane writes it
+          sts_v4(xb + m * kXRowBytes + ((lane ^ (m & 7)) * 16), o);
+        }
+        fence_proxy_async_smem();  // the slot's next TMA fill comes after these writes
+        __syncwarp();
+      }
       const int k0 = (sb + li) * kBoxRows;
       const int gbase = k0 / a.G;
       const int steps = min(kBoxRows, a.K - k0) / 16;  // K is a multiple of 16
@@ -267,9 +294,15 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
         for (int mt = 0; mt < MT; ++mt) {
           uint32_t b0 = 0u, b1 = 0u;
           if (xok[mt]) {
-            const uint32_t xa = base + a.x_off + xrow[mt] + s * 32;
-            b0 = lds_u32(xa);
-            b1 = lds_u32(xa + 16);
+            if (PERM) {  // chunks 2s and 2s+1 of token 8mt+g, rotated by g
+              const uint32_t xa = base + a.x_off + xrow[mt];
+              b0 = lds_u32(xa + ((static_cast<uint32_t>(2 * s) ^ g) << 4));
+              b1 = lds_u32(xa + ((static_cast<uint32_t>(2 * s + 1) ^ g) << 4));
+            } else {
+              const uint32_t xa = base + a.x_off + xrow[mt] + s * 32;
+              b0 = lds_u32(xa);
+              b1 = lds_u32(xa + 16);
+            }
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -459,13 +492,13 @@ bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p) {
   return true;
 }
 
-template <int MT, int C, bool RAW>
+template <int MT, int C, bool RAW, bool PERM>
 int launch_strip_t(const StripMaps& maps, const StripArgs& args, int tiles, size_t smem, cudaStream_t stream) {
   const int ks = args.ksplit;
   static std::atomic<bool> configured[64];  // zero-initialised (static storage)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ASHQK_ERR_CUDA;
-  auto kernel = gemv_strip_kernel<MT, C, RAW>;
+  auto kernel = gemv_strip_kernel<MT, C, RAW, PERM>;
   if (!configured[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
@@ -506,10 +539,20 @@ bool raw_unpack() {
   return on;
 }
 
+// Permuted k order (env ASHQK_STRIP_PERM=1, together with ASHQK_STRIP_RAW=1).
+bool perm_rows() {
+  static const bool on = [] {
+    const char* e = std::getenv("ASHQK_STRIP_PERM");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
 template <int MT, int C>
 int launch_strip(const StripMaps& maps, const StripArgs& args, int tiles, size_t smem, cudaStream_t stream) {
-  return raw_unpack() ? launch_strip_t<MT, C, true>(maps, args, tiles, smem, stream)
-                      : launch_strip_t<MT, C, false>(maps, args, tiles, smem, stream);
+  if (!raw_unpack()) return launch_strip_t<MT, C, false, false>(maps, args, tiles, smem, stream);
+  return perm_rows() ? launch_strip_t<MT, C, true, true>(maps, args, tiles, smem, stream)
+                     : launch_strip_t<MT, C, true, false>(maps, args, tiles, smem, stream);
 }
 
 }  // namespace

@@ -220,6 +220,11 @@ __device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
   return v;
 }
 
+__device__ __forceinline__ void sts_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 // ---- thread-block clusters ---------------------------------------------------
 
 __device__ __forceinline__ uint32_t cluster_rank() {

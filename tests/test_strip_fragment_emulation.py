@@ -1,0 +1,150 @@
+"""Lane-level emulation of one 16-row step of the column-strip GEMV consumer (``csrc/gemv_strip.cu``).
+
+Emulates, on the bytes of a shared-memory stage, exactly what each of a warp's 32 lanes loads and
+computes: the weight-row offsets, the byte permutes (``prmt``) and nibble masks that build the
+mma.sync A fragments, the x loads that build the B fragments, and -- for the PERM variant -- the
+per-stage rewrite of x (k permuted inside each 16-value block, 16-byte chunks rotated by token).
+The fragments of all lanes are then assembled into the m16n8k16 A (16 x 16) and B (16 x 8)
+matrices following the PTX fragment layout, multiplied, and compared with the dot products the
+kernel's epilogue assumes: row r of mma j is column j (r < 8) or j + 4 (r >= 8) of word r % 8,
+column n is token 8 * mt + n. Values are the RAW variant's magic-number halves (1024 + q for
+columns 0, 1, 4, 5 of a word, 1024 + 16 q for 2, 3, 6, 7); the nibble selection is the same in the
+zero-point-subtracting variant.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import awq_oracle as O
+
+X_ROW_BYTES = 512  # one token's 256 fp16 x values per stage
+
+
+def prmt(a: int, b: int, sel: int) -> int:
+    src = [(a >> (8 * i)) & 0xFF for i in range(4)] + [(b >> (8 * i)) & 0xFF for i in range(4)]
+    return sum(src[(sel >> (4 * i)) & 7] << (8 * i) for i in range(4))
+
+
+def lop3_and_or(v: int, mask: int, magic: int) -> int:
+    return (v & mask) | magic
+
+
+def unpack_raw(T: int):
+    T8 = T >> 8
+    return [lop3_and_or(T, 0x000F000F, 0x64006400), lop3_and_or(T, 0x00F000F0, 0x64006400),
+            lop3_and_or(T8, 0x000F000F, 0x64006400), lop3_and_or(T8, 0x00F000F0, 0x64006400)]
+
+
+def halves(u32: int):
+    lo, hi = np.array([u32 & 0xFFFF, u32 >> 16], dtype=np.uint16).view(np.float16)
+    return float(lo), float(hi)
+
+
+class Stage:
+    """Shared memory of one stage: weights [256 rows][8 words], then x [M][256] fp16."""
+
+    def __init__(self, words: np.ndarray, x: np.ndarray):
+        self.words = words.astype(np.uint32)            # [256, 8]
+        self.x = x.astype(np.float16).view(np.uint16)   # [M, 256] bit patterns
+        self.M = x.shape[0]
+
+    def w_at(self, byte_off: int) -> int:
+        return int(self.words.reshape(-1)[byte_off // 4])
+
+    def x_u32(self, byte_off: int) -> int:
+        flat = self.x.reshape(-1)
+        i = byte_off // 2
+        return int(flat[i]) | (int(flat[i + 1]) << 16)
+
+    def x_prep(self):
+        """The PERM rewrite: lane l permutes chunk l of row m and stores it at chunk l ^ (m & 7)."""
+        for m in range(self.M):
+            row = self.x[m].copy()
+            chunks = row.view(np.uint32).reshape(32, 4)
+            out = np.empty_like(chunks)
+            for lane in range(32):
+                vx, vy, vz, vw = (int(c) for c in chunks[lane])
+                o = [prmt(vx, vz, 0x5410), prmt(vx, vz, 0x7632), prmt(vy, vw, 0x5410), prmt(vy, vw, 0x7632)]
+                out[lane ^ (m & 7)] = o
+            self.x[m] = out.reshape(-1).view(np.uint16)
+
+
+def emulate_step(stage: Stage, s: int, perm: bool, mt_count: int):
+    """Assemble, for every mma j and token tile mt, the A and B matrices the warp feeds mma.sync."""
+    A = np.full((4, 16, 16), np.nan)
+    B = np.full((mt_count, 16, 8), np.nan)
+    for lane in range(32):
+        g, t = lane >> 2, lane & 3
+        roff = [((t + 4 * q) if perm else (2 * t + (q & 1) + 8 * (q >> 1))) * 32 + 4 * g for q in range(4)]
+        w = [stage.w_at(s * 16 * 32 + r) for r in roff]
+        oa, ob = unpack_raw(prmt(w[0], w[1], 0x6420)), unpack_raw(prmt(w[0], w[1], 0x7531))
+        oc, od = unpack_raw(prmt(w[2], w[3], 0x6420)), unpack_raw(prmt(w[2], w[3], 0x7531))
+        for j in range(4):
+            sl = ((j & 1) << 1) | (j >> 1)
+            regs = [oa[sl], ob[sl], oc[sl], od[sl]]
+            for reg, (row, kb) in zip(regs, [(g, 2 * t), (g + 8, 2 * t), (g, 2 * t + 8), (g + 8, 2 * t + 8)]):
+                assert np.isnan(A[j, row, kb]) and np.isnan(A[j, row, kb + 1])
+                A[j, row, kb], A[j, row, kb + 1] = halves(reg)
+        for mt in range(mt_count):
+            tok = 8 * mt + g
+            b0 = b1 = 0
+            if tok < stage.M:
+                xrow = tok * X_ROW_BYTES + 4 * t
+                if perm:
+                    b0 = stage.x_u32(xrow + (((2 * s) ^ g) << 4))
+                    b1 = stage.x_u32(xrow + (((2 * s + 1) ^ g) << 4))
+                else:
+                    b0 = stage.x_u32(xrow + s * 32)
+                    b1 = stage.x_u32(xrow + s * 32 + 16)
+            for reg, kb in ((b0, 2 * t), (b1, 2 * t + 8)):
+                assert np.isnan(B[mt, kb, g])
+                B[mt, kb, g], B[mt, kb + 1, g] = halves(reg)
+    assert not np.isnan(A).any() and not np.isnan(B).any()
+    return A, B
+
+
+@pytest.mark.parametrize("perm", [False, True])
+@pytest.mark.parametrize("m", [1, 4, 9, 16])
+def test_fragments_compute_the_strip_dot_products(perm, m):
+    rng = np.random.default_rng(1000 * m + perm)
+    k0, n_words = 0, 8
+    q = rng.integers(0, 16, (256, 8 * n_words))
+    words = O.pack_awq(q.astype(np.int32)).view(np.uint32)      # [256, 8]: the stage's weight box
+    x = rng.standard_normal((m, 256)).astype(np.float16)
+    stage = Stage(words, x)
+    if perm:
+        stage.x_prep()
+    mt_count = 2 if m > 8 else 1
+    low = np.array([c % 4 < 2 for c in range(8)])
+    magic = np.where(np.tile(low, n_words), 1024 + q, 1024 + 16 * q).astype(np.float64)  # [256, 64]
+    xf = x.astype(np.float64)
+    for s in range(16):
+        A, B = emulate_step(stage, s, perm, mt_count)
+        for j in range(4):
+            for mt in range(mt_count):
+                C = A[j] @ B[mt]                                  # [16 mma rows, 8 tokens]
+                for r in range(16):
+                    col = 8 * (r % 8) + j + (4 if r >= 8 else 0)
+                    for n in range(8):
+                        tok = 8 * mt + n
+                        want = 0.0 if tok >= m else float(magic[k0 + 16 * s:k0 + 16 * s + 16, col]
+                                                            @ xf[tok, 16 * s:16 * s + 16])
+                        assert C[r, n] == pytest.approx(want, rel=1e-12, abs=1e-9), (perm, s, j, mt, r, n)
+
+
+def test_perm_reads_are_bank_conflict_free():
+    """Weight loads (per q) and x loads (per mt, for a full 8-token fragment) of the PERM variant
+    hit 32 distinct banks; the original order puts lanes t and t + 2 on the same banks."""
+    def banks(offsets):
+        return [(o // 4) % 32 for o in offsets]
+
+    for q in range(4):
+        perm = banks([(t + 4 * q) * 32 + 4 * g for g in range(8) for t in range(4)])
+        orig = banks([(2 * t + (q & 1) + 8 * (q >> 1)) * 32 + 4 * g for g in range(8) for t in range(4)])
+        assert len(set(perm)) == 32 and len(set(orig)) == 16
+    for s in range(16):
+        perm = banks([g * X_ROW_BYTES + 4 * t + (((2 * s) ^ g) << 4) for g in range(8) for t in range(4)])
+        orig = banks([g * X_ROW_BYTES + 4 * t + s * 32 for g in range(8) for t in range(4)])
+        assert len(set(perm)) == 32 and len(set(orig)) == 4
