@@ -148,3 +148,41 @@ def test_perm_reads_are_bank_conflict_free():
         perm = banks([g * X_ROW_BYTES + 4 * t + (((2 * s) ^ g) << 4) for g in range(8) for t in range(4)])
         orig = banks([g * X_ROW_BYTES + 4 * t + s * 32 for g in range(8) for t in range(4)])
         assert len(set(perm)) == 32 and len(set(orig)) == 4
+
+
+NIBBLE_OF_COL = (0, 4, 1, 5, 2, 6, 3, 7)  # kAwqNibbleOfCol in csrc/awq_unpack.cuh
+
+
+@pytest.mark.parametrize("perm", [False, True])
+def test_raw_flush_recovers_q_minus_z(perm):
+    """The RAW epilogue per lane: C fragments of mma j scaled by f_j, minus (c + z) times the group's
+    sum of x taken from the ones-mma's c0 / c1, give sum x (q - z) for the lane's columns and tokens
+    (one group = one 16-row step here, zero points from the packed qzeros word of word g)."""
+    rng = np.random.default_rng(5 + perm)
+    m = 8
+    q = rng.integers(0, 16, (256, 64))
+    z = rng.integers(0, 16, (1, 64))
+    zwords = [int(w) for w in O.pack_awq(z.astype(np.int32)).view(np.uint32)[0]]
+    stage = Stage(O.pack_awq(q.astype(np.int32)).view(np.uint32), rng.standard_normal((m, 256)).astype(np.float16))
+    xf = stage.x.view(np.float16).astype(np.float64).copy()  # before the PERM rewrite
+    if perm:
+        stage.x_prep()
+    for s in (0, 7, 15):
+        A, B = emulate_step(stage, s, perm, 1)
+        ones = np.ones((16, 16))
+        SX = ones @ B[0]                                   # the ones-mma: every row holds sum_k x
+        for lane in range(32):
+            g, t = lane >> 2, lane & 3
+            zk = [((zwords[g] >> (4 * NIBBLE_OF_COL[c])) & 15) + (64.0 if c & 2 else 1024.0) for c in range(8)]
+            psx = (SX[g, 2 * t], SX[g, 2 * t + 1])         # c0, c1 of the ones-mma
+            for j in range(4):
+                f = 1.0 if j < 2 else 1 / 16
+                C = A[j] @ B[0]
+                frag = [(C[g, 2 * t], j, 0), (C[g, 2 * t + 1], j, 1), (C[g + 8, 2 * t], 4 + j, 0),
+                        (C[g + 8, 2 * t + 1], 4 + j, 1)]
+                for val, c, tsel in frag:
+                    got = val * f - zk[c] * psx[tsel]
+                    col, tok = 8 * g + c, 2 * t + tsel
+                    ks = slice(16 * s, 16 * s + 16)
+                    want = float(xf[tok, ks] @ (q[ks, col] - z[0, col]))
+                    assert got == pytest.approx(want, rel=1e-9, abs=1e-6), (perm, s, lane, j, c)
