@@ -206,6 +206,8 @@ class P2PAllReduce:
                                                     ctypes.c_int64, vp]
         self._lib, self.group = lib, group
         self.rank, self.world = _world(group)
+        if self.world > 8:
+            raise ValueError("P2PAllReduce handles at most 8 ranks (one NVLink domain of B200s)")
         self.max_elems = int(max_elems)
         size = ctypes.c_size_t(0)
         if lib.ashqk_p2p_region_bytes(self.max_elems, ctypes.byref(size)) != 0:
