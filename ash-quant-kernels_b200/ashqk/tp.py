@@ -185,8 +185,13 @@ class P2PAllReduce:
     rounded once. ``close()`` (collective) releases the regions.
     """
 
-    def __init__(self, group=None, max_elems: int = 1 << 16, lib=None):
-        """``lib``: the loaded C library (default: the package's own; tests pass a fake)."""
+    def __init__(self, group=None, max_elems: int = 1 << 16, lib=None, protocol: str = "oneshot"):
+        """``protocol``: "oneshot" (copy, fenced flag, peer loads; one CTA) or "ll" (8-byte
+        data + epoch lines pushed to the peers, one CTA per 1024 elements, max_elems <= 65536).
+        ``lib``: the loaded C library (default: the package's own; tests pass a fake)."""
+        if protocol not in ("oneshot", "ll"):
+            raise ValueError("protocol: 'oneshot' or 'll'")
+        self.protocol = protocol
         import ctypes
 
         self._ct = ctypes
@@ -202,16 +207,19 @@ class P2PAllReduce:
         lib.ashqk_p2p_import.argtypes = [vp, ctypes.POINTER(vp)]
         lib.ashqk_p2p_close.argtypes = [vp]
         lib.ashqk_get_device_errors.argtypes = [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]
-        lib.ashqk_allreduce_f16_oneshot.argtypes = [vp, vp, ctypes.c_int64, vp, ctypes.c_int, ctypes.c_int,
-                                                    ctypes.c_int64, vp]
+        for name in ("ashqk_allreduce_f16_oneshot", "ashqk_allreduce_f16_ll"):
+            getattr(lib, name).argtypes = [vp, vp, ctypes.c_int64, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int64, vp]
+        lib.ashqk_p2p_ll_region_bytes.argtypes = [ctypes.c_int64, ctypes.POINTER(ctypes.c_size_t)]
+        self._region_bytes = lib.ashqk_p2p_ll_region_bytes if protocol == "ll" else lib.ashqk_p2p_region_bytes
+        self._reduce = lib.ashqk_allreduce_f16_ll if protocol == "ll" else lib.ashqk_allreduce_f16_oneshot
         self._lib, self.group = lib, group
         self.rank, self.world = _world(group)
         if self.world > 8:
             raise ValueError("P2PAllReduce handles at most 8 ranks (one NVLink domain of B200s)")
         self.max_elems = int(max_elems)
         size = ctypes.c_size_t(0)
-        if lib.ashqk_p2p_region_bytes(self.max_elems, ctypes.byref(size)) != 0:
-            raise ValueError("max_elems must be a positive multiple of 8")
+        if self._region_bytes(self.max_elems, ctypes.byref(size)) != 0:
+            raise ValueError("max_elems must be a positive multiple of 8 (at most 65536 for protocol 'll')")
         region = vp()
         if lib.ashqk_p2p_alloc(size.value, ctypes.byref(region)) != 0:
             raise RuntimeError("ashqk: cannot allocate the all-reduce region")
@@ -268,11 +276,10 @@ class P2PAllReduce:
             out = torch.empty_like(t)
         assert (out.dtype == torch.float16 and out.device == t.device and out.is_contiguous()
                 and out.numel() == t.numel()), "out: fp16, contiguous, same device and size as t"
-        rc = self._lib.ashqk_allreduce_f16_oneshot(t.data_ptr(), out.data_ptr(), t.numel(),
-                                                   self._regions_dev.data_ptr(), self.rank, self.world,
-                                                   self.max_elems, torch.cuda.current_stream().cuda_stream)
+        rc = self._reduce(t.data_ptr(), out.data_ptr(), t.numel(), self._regions_dev.data_ptr(), self.rank,
+                          self.world, self.max_elems, torch.cuda.current_stream().cuda_stream)
         if rc != 0:
-            raise RuntimeError(f"ashqk_allreduce_f16_oneshot failed ({rc})")
+            raise RuntimeError(f"ashqk all-reduce ({self.protocol}) failed ({rc})")
         return out
 
     def check(self) -> None:

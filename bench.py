@@ -593,13 +593,14 @@ def run_gpu(args):
             print(json.dumps({"prefill": res}), flush=True)
         return
     stack = make_stack(world, rank, device, args.layers)
-    # Tensor-parallel reductions: NCCL by default, the NVLink one-shot kernel with
-    # ASHQK_TP_ALLREDUCE=p2p.
+    # Tensor-parallel reductions: NCCL by default, the NVLink kernels with
+    # ASHQK_TP_ALLREDUCE=p2p (one-shot) or =ll (low-latency lines).
     p2p = None
-    if world > 1 and os.environ.get("ASHQK_TP_ALLREDUCE", "nccl") == "p2p":
+    tp_reduce = os.environ.get("ASHQK_TP_ALLREDUCE", "nccl")
+    if world > 1 and tp_reduce in ("p2p", "ll"):
         from ashqk import tp
 
-        p2p = tp.P2PAllReduce(group=group, max_elems=4 * 4096)
+        p2p = tp.P2PAllReduce(group=group, max_elems=4 * 4096, protocol="ll" if tp_reduce == "ll" else "oneshot")
     results = {}
     graphs = {}
     for m in (1, 4):

@@ -230,6 +230,20 @@ ASHQK_API int ashqk_p2p_close(void* ptr);
 ASHQK_API int ashqk_allreduce_f16_oneshot(const void* in, void* out, int64_t n, const void* regions_dev, int rank,
                                           int world, int64_t max_elems, void* stream);
 
+/*
+ * Low-latency variant of the same all-reduce: every rank pushes each pair of
+ * fp16 values into every peer's region as one 8-byte line together with the
+ * call's epoch (no fence, no peer-load round trip) and polls its own region;
+ * one CTA per 1024 elements (at most 64 CTAs). Regions are sized by
+ * ashqk_p2p_ll_region_bytes (max_elems <= 65536) and set up exactly as for
+ * ashqk_allreduce_f16_oneshot (allocate, export, import, pointer array); a
+ * region serves one of the two variants. Same sum (fp32, rank order, one
+ * rounding), same ~2 s peer limit and sticky device error bit 3.
+ */
+ASHQK_API int ashqk_p2p_ll_region_bytes(int64_t max_elems, size_t* bytes);
+ASHQK_API int ashqk_allreduce_f16_ll(const void* in, void* out, int64_t n, const void* regions_dev, int rank,
+                                     int world, int64_t max_elems, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -143,3 +143,97 @@ def test_missing_peer_times_out(lib):
     assert _call(lib, regs, a, out) == 0
     torch.cuda.synchronize()
     assert bool((out == 4.0).all()) and _errors(lib) == 0
+
+
+# ---- low-latency variant (ashqk_allreduce_f16_ll) -----------------------------------------------
+# Written after the last GPU session; these run when ASHQK_TEST_LL=1 until the variant has passed
+# on a GPU once.
+import os  # noqa: E402
+
+ll_pending = pytest.mark.skipif(os.environ.get("ASHQK_TEST_LL") != "1",
+                                reason="LL all-reduce awaiting its first GPU run (set ASHQK_TEST_LL=1)")
+MAX_RANKS = 8
+
+
+class _LLRegions:
+    """Rank 0's LL region and the host-played rank 1's, both on this GPU."""
+
+    def __init__(self, lib, max_elems):
+        lib.ashqk_p2p_ll_region_bytes.argtypes = [ctypes.c_int64, ctypes.POINTER(ctypes.c_size_t)]
+        lib.ashqk_allreduce_f16_ll.argtypes = lib.ashqk_allreduce_f16_oneshot.argtypes
+        size = ctypes.c_size_t(0)
+        assert lib.ashqk_p2p_ll_region_bytes(max_elems, ctypes.byref(size)) == 0
+        self.max_elems, self.pairs = max_elems, max_elems // 2
+        self.r = [torch.zeros(size.value, dtype=torch.uint8, device="cuda") for _ in range(2)]
+        self.ptrs = torch.tensor([t.data_ptr() for t in self.r], dtype=torch.int64, device="cuda")
+
+    def lines(self, dst, parity, src):
+        inbox = self.r[dst][HEADER:].view(torch.int64).view(2, MAX_RANKS, self.pairs)
+        return inbox[parity, src]
+
+    def counters(self, q):
+        return self.r[q][:HEADER].view(torch.int32)
+
+
+def _pack_lines(t, epoch):
+    data = t.reshape(-1).view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    return data | (epoch << 32)
+
+
+def _call_ll(lib, regs, x, out, rank=0, world=2):
+    return lib.ashqk_allreduce_f16_ll(x.data_ptr(), out.data_ptr(), x.numel(), regs.ptrs.data_ptr(), rank, world,
+                                      regs.max_elems, torch.cuda.current_stream().cuda_stream)
+
+
+@ll_pending
+def test_ll_protocol_and_sum(lib):
+    assert _errors(lib, clear=True) & PEER_BIT == 0
+    regs = _LLRegions(lib, 1 << 15)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1)
+    for epoch, shape in enumerate([(4, 4096), (1, 4096), (8, 4096), (2, 8)], start=1):
+        n = shape[0] * shape[1]
+        ctas = -(-(n // 2) // 512)
+        a = (torch.randn(shape, device="cuda", generator=g) * 2).half()
+        b = (torch.randn(shape, device="cuda", generator=g) * 2).half()
+        # Every CTA keeps its own epoch (calls of different sizes run different CTA counts): the
+        # pairs of CTA c travel with epoch counters[c] + 1 in slot parity (counters[c] + 1) & 1.
+        ep = [int(v) + 1 for v in regs.counters(0)[:ctas].tolist()]
+        pa, pb = _pack_lines(a, 0), _pack_lines(b, 0)
+        for c, e in enumerate(ep):
+            sl = slice(512 * c, min(512 * (c + 1), n // 2))
+            regs.lines(0, e & 1, 1)[sl] = pb[sl] | (e << 32)             # the peer's pushed lines
+        out = torch.full_like(a, float("nan"))
+        assert _call_ll(lib, regs, a, out) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(out, (a.float() + b.float()).half()), epoch
+        assert regs.counters(0)[:ctas].tolist() == ep
+        for c, e in enumerate(ep):                                       # pushed to the peer
+            sl = slice(512 * c, min(512 * (c + 1), n // 2))
+            assert torch.equal(regs.lines(1, e & 1, 0)[sl], pa[sl] | (e << 32)), (epoch, c)
+    a = torch.randn(8, 512, device="cuda", generator=g).half()
+    ref = a.clone()
+    assert _call_ll(lib, regs, a, a, world=1) == 0                       # world 1: a copy, in place
+    torch.cuda.synchronize()
+    assert torch.equal(a, ref) and _errors(lib) & PEER_BIT == 0
+
+
+@ll_pending
+def test_ll_missing_peer_times_out(lib):
+    regs = _LLRegions(lib, 1024)
+    a = torch.ones(1024, dtype=torch.float16, device="cuda")
+    out = torch.full_like(a, -7.0)
+    _errors(lib, clear=True)
+    t0 = time.time()
+    assert _call_ll(lib, regs, a, out) == 0                               # no line ever arrives
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    try:
+        assert _errors(lib) & PEER_BIT and 0.5 < waited < 30, waited
+        assert bool((out == -7.0).all())
+        t0 = time.time()
+        assert _call_ll(lib, regs, a, out) == 0                           # sticky: returns at once
+        torch.cuda.synchronize()
+        assert time.time() - t0 < 0.5 and int(regs.counters(0)[0]) == 1
+    finally:
+        _errors(lib, clear=True)

@@ -150,7 +150,7 @@ def test_tp_mlp_rank_shapes(layer, m, world):
     assert e <= 2 * e_cublas + 1e-5, (e, e_cublas)
 
 
-def _p2p_worker(rank, world, port):
+def _p2p_worker(rank, world, port, protocol="oneshot"):
     from datetime import timedelta
 
     import torch.distributed as dist
@@ -162,7 +162,7 @@ def _p2p_worker(rank, world, port):
     try:
         from ashqk import tp
 
-        ar = tp.P2PAllReduce(max_elems=1 << 16)
+        ar = tp.P2PAllReduce(max_elems=1 << 16, protocol=protocol)
 
         def data(trial, r, shape=(4, 4096)):
             g = torch.Generator(device=dev)
@@ -214,8 +214,14 @@ def _p2p_worker(rank, world, port):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2+ GPUs")
-def test_p2p_allreduce():
+@pytest.mark.parametrize("protocol", [
+    "oneshot",
+    pytest.param("ll", marks=pytest.mark.skipif(os.environ.get("ASHQK_TEST_LL") != "1",
+                                                reason="LL all-reduce awaiting its first GPU run")),
+])
+def test_p2p_allreduce(protocol):
     import torch.multiprocessing as mp
 
     world = min(torch.cuda.device_count(), 8)
-    mp.start_processes(_p2p_worker, args=(world, _free_port()), nprocs=world, start_method="spawn", join=True)
+    mp.start_processes(_p2p_worker, args=(world, _free_port(), protocol), nprocs=world, start_method="spawn",
+                       join=True)

@@ -102,3 +102,66 @@ def test_one_slot_would_be_wrong():
     # stages call e + 1 over the partial a slower peer has not read yet.
     with pytest.raises(AssertionError, match="saw"):
         _explore(2, 2, nslots=1)
+
+
+# ---- low-latency variant (``allreduce_ll_kernel``): the epoch travels with the data ----------
+
+
+def _explore_ll(world, calls, nslots=2):
+    """Per call and rank: bump the epoch; push (rank, epoch) into slot epoch % nslots of every
+    peer's inbox line for this rank (one action per peer); then for each peer, in rank order, wait
+    until the own inbox line from that peer carries the epoch and read it. The check: every read
+    sees exactly (peer, epoch) -- the line is never overwritten by the peer's next-but-one call
+    before it is read -- and no state is stuck."""
+    acts = []
+    for r in range(world):
+        a = [("bump",)] + [("push", q) for q in range(world) if q != r] + [("pull", q) for q in range(world) if q != r]
+        acts.append(a)
+    # state: per rank (call, action index, epoch); inbox[dst][src][slot] = (src, epoch) or None
+    init = (tuple((0, 0, 0) for _ in range(world)),
+            tuple(tuple(tuple(None for _ in range(nslots)) for _ in range(world)) for _ in range(world)))
+    seen, stack = {init}, [init]
+    while stack:
+        ranks, inbox = stack.pop()
+        moved = False
+        for r in range(world):
+            call, ai, epoch = ranks[r]
+            if call == calls:
+                continue
+            act = acts[r][ai]
+            box = [[list(sl) for sl in dst] for dst in inbox]
+            nepoch = epoch
+            if act[0] == "bump":
+                nepoch = epoch + 1
+            elif act[0] == "push":
+                box[act[1]][r][epoch % nslots] = (r, epoch)
+            elif act[0] == "pull":
+                line = inbox[r][act[1]][epoch % nslots]
+                if line is None or line[1] != epoch:
+                    assert line is None or line[1] < epoch, f"rank {r} call {epoch} saw a newer line {line}"
+                    continue  # still waiting: the epoch is not there yet
+            nai, ncall = ai + 1, call
+            if nai == len(acts[r]):
+                nai, ncall = 0, call + 1
+            nr = list(ranks)
+            nr[r] = (ncall, nai, nepoch)
+            state = (tuple(nr), tuple(tuple(tuple(sl) for sl in dst) for dst in box))
+            moved = True
+            if state not in seen:
+                seen.add(state)
+                stack.append(state)
+        if not moved:
+            assert all(c == calls for c, _, _ in ranks), f"stuck: {ranks}"
+    return len(seen)
+
+
+@pytest.mark.parametrize("world,calls", [(2, 1), (2, 3), (2, 5), (3, 3), (4, 2)])
+def test_ll_lines_are_read_before_they_are_overwritten(world, calls):
+    assert _explore_ll(world, calls) > 1
+
+
+def test_ll_one_slot_would_lose_lines():
+    # With one slot a fast rank's next call overwrites a line a slow peer has not read yet, and the
+    # slow peer then waits for an epoch that is gone.
+    with pytest.raises(AssertionError):
+        _explore_ll(2, 3, nslots=1)
