@@ -120,9 +120,13 @@ def row_parallel_linear(x_local: torch.Tensor, qweight, qzeros, scales, group=No
     ``P2PAllReduce`` of the same group) replaces NCCL for partials it can hold;
     it too sums in fp32 with one rounding.
     """
+    _, world = _world(group)
+    if world > 1 and linear is None and allreduce is not None and allreduce.protocol == "ll":
+        y = allreduce.fused_linear(x_local, qweight, qzeros, scales)
+        if y is not None:  # GEMV and all-reduce in one kernel
+            return y
     linear = linear or w4a16_linear
     y = linear(x_local, qweight, qzeros, scales)
-    _, world = _world(group)
     if world == 1:
         return y
     if allreduce is not None and y.is_contiguous() and y.numel() % 8 == 0 and y.numel() <= allreduce.max_elems:
@@ -209,6 +213,9 @@ class P2PAllReduce:
         lib.ashqk_get_device_errors.argtypes = [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]
         for name in ("ashqk_allreduce_f16_oneshot", "ashqk_allreduce_f16_ll"):
             getattr(lib, name).argtypes = [vp, vp, ctypes.c_int64, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int64, vp]
+        i64, ci = ctypes.c_int64, ctypes.c_int
+        lib.ashqk_w4a16_gemv_allreduce.argtypes = [vp, i64, vp, i64, vp, i64, vp, i64, vp, i64, ci, ci, ci, ci, vp, ci,
+                                                   ci, i64, vp]
         lib.ashqk_p2p_ll_region_bytes.argtypes = [ctypes.c_int64, ctypes.POINTER(ctypes.c_size_t)]
         self._region_bytes = lib.ashqk_p2p_ll_region_bytes if protocol == "ll" else lib.ashqk_p2p_region_bytes
         self._reduce = lib.ashqk_allreduce_f16_ll if protocol == "ll" else lib.ashqk_allreduce_f16_oneshot
@@ -281,6 +288,29 @@ class P2PAllReduce:
         if rc != 0:
             raise RuntimeError(f"ashqk all-reduce ({self.protocol}) failed ({rc})")
         return out
+
+    def fused_linear(self, x, qweight, qzeros, scales) -> Optional[torch.Tensor]:
+        """Row-parallel layer in one kernel (protocol "ll"): the sum over ranks of
+        ``x @ W_shard``, or None when the fused kernel does not take the problem (the caller
+        then runs the GEMV and this all-reduce). x: [M, K_shard] fp16, M <= 16."""
+        if self.protocol != "ll" or x.dim() != 2 or x.dtype != torch.float16 or not x.is_cuda:
+            return None
+        m, k = x.shape
+        n = qweight.shape[1] * 8
+        if m > 16 or m * n > self.max_elems or x.stride(1) != 1 or any(t.stride(1) != 1 for t in
+                                                                        (qweight, qzeros, scales)):
+            return None
+        y = torch.empty(m, n, dtype=torch.float16, device=x.device)
+        rc = self._lib.ashqk_w4a16_gemv_allreduce(
+            x.data_ptr(), x.stride(0), qweight.data_ptr(), qweight.stride(0), qzeros.data_ptr(), qzeros.stride(0),
+            scales.data_ptr(), scales.stride(0), y.data_ptr(), y.stride(0), m, n, k, k // scales.shape[0],
+            self._regions_dev.data_ptr(), self.rank, self.world, self.max_elems,
+            torch.cuda.current_stream().cuda_stream)
+        if rc == 2:  # ASHQK_ERR_UNSUPPORTED: nothing launched
+            return None
+        if rc != 0:
+            raise RuntimeError(f"ashqk_w4a16_gemv_allreduce failed ({rc})")
+        return y
 
     def check(self) -> None:
         """Raise if a call on this device gave up waiting for a peer (the results since are invalid)."""

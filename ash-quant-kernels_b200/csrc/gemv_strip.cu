@@ -34,6 +34,7 @@
 #include <cstdlib>
 
 #include "awq_unpack.cuh"
+#include "ll_lines.cuh"
 #include "sm100.cuh"
 
 namespace ashqk {
@@ -57,11 +58,50 @@ struct StripArgs {
   int stage_bytes;   // bytes of one ring slot (multiple of 128)
   int x_off, s_off, z_off;  // byte offsets of x, scales, zeros inside a slot
   uint32_t tx_bytes;        // transaction bytes per stage
+  LLPeers ll;               // regions != nullptr: sum y over the ranks before storing it
 };
 
 struct StripMaps {
   CUtensorMap qw, x, s, z;
 };
+
+// Sum over the S CTAs of the cluster (fixed rank order; S == 1: the own tile)
+// of column c of token m's partial tile.
+__device__ __forceinline__ float strip_tile_value(const float* tile_sum, int m, int c, int S) {
+  if (S == 1) return tile_sum[m * kStripCols + c];
+  float pq[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    pq[q] = q < S ? ld_shared_cluster_f32(map_shared_rank(const_cast<float*>(tile_sum) + m * kStripCols + c, q)) : 0.f;
+  return ((pq[0] + pq[1]) + pq[2]) + pq[3];
+}
+
+// Row-parallel epilogue: this rank's fp16 partial of columns [c_lo, c_hi) of
+// the strip (pairs) goes to every peer as low-latency lines (ll_lines.cuh);
+// the stored y is the fp32 sum of all ranks' fp16 partials in rank order,
+// rounded once -- the same value an unfused GEMV followed by the LL or one-shot
+// all-reduce produces.
+template <typename Args>
+__device__ void strip_allreduce_store(const Args& a, const float* tile_sum, int col0, int c_lo, int c_hi, int S,
+                                      unsigned int epoch, int nthreads) {
+  const int pairs_per_row = (c_hi - c_lo) / 2;
+  const int total = a.M * pairs_per_row;
+  for (int i = threadIdx.x; i < total; i += nthreads) {
+    const int m = i / pairs_per_row, c = c_lo + 2 * (i % pairs_per_row);
+    if (col0 + c >= a.N) continue;
+    const __half2 h = __floats2half2_rn(strip_tile_value(tile_sum, m, c, S), strip_tile_value(tile_sum, m, c + 1, S));
+    ll_push(a.ll, epoch, static_cast<long long>(m) * (a.N / 2) + (col0 + c) / 2, *reinterpret_cast<const unsigned int*>(&h));
+  }
+  bool failed = false;
+  for (int i = threadIdx.x; i < total && !failed; i += nthreads) {
+    const int m = i / pairs_per_row, c = c_lo + 2 * (i % pairs_per_row);
+    if (col0 + c >= a.N) continue;
+    const __half2 h = __floats2half2_rn(strip_tile_value(tile_sum, m, c, S), strip_tile_value(tile_sum, m, c + 1, S));
+    const float2 v = ll_pull_sum(a.ll, epoch, static_cast<long long>(m) * (a.N / 2) + (col0 + c) / 2,
+                                 *reinterpret_cast<const unsigned int*>(&h), failed);
+    if (!failed) *reinterpret_cast<__half2*>(a.y + m * a.y_ld + col0 + c) = __floats2half2_rn(v.x, v.y);
+  }
+}
 
 // RAW: feed the magic-number halves (1024 + q, 1024 + 16 q) to the mma without
 // subtracting the zero point per weight, accumulate each group's sum of x with
@@ -78,7 +118,11 @@ struct StripMaps {
 // (x0, x4, x1, x5, x2, x6, x3, x7, x8, x12, ...), and token m's 16-byte chunk
 // c moves to chunk c ^ (m & 7) so that the 8 tokens of an mma fragment, 512
 // bytes apart, also read distinct banks.
-template <int MT, int C, bool RAW, bool PERM>
+//
+// FUSED: row-parallel tensor parallelism -- y is this rank's partial over its K
+// shard, summed over the ranks in the epilogue (strip_allreduce_store) before
+// it is stored.
+template <int MT, int C, bool RAW, bool PERM, bool FUSED>
 __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_constant__ StripMaps maps,
                                                                   const StripArgs a) {
   extern __shared__ unsigned char smem_raw[];
@@ -87,6 +131,8 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
   __shared__ uint64_t full[kMaxStages];
   __shared__ uint64_t empty[kMaxStages];
   __shared__ int abort_flag;
+  __shared__ unsigned int ll_epoch;
+  __shared__ int ll_skip;
 
   const int strip = blockIdx.x;
   const int col0 = strip * kStripCols;
@@ -357,9 +403,21 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
     for (int w = 0; w < C; ++w) v += red[(w * kTok + m) * kRow + c];
     tile_sum[m * kStripCols + c] = v;
   }
+  constexpr bool fused = FUSED;
+  if (fused && threadIdx.x == 0) {  // a consumer thread: past griddepcontrol.wait
+    ll_skip = ll_sticky_failure();
+    ll_epoch = ll_call_epoch(a.ll);
+  }
   if (a.ksplit == 1) {
     __syncthreads();
     if (failed) return;
+    if (fused) {
+      if (ll_skip) return;
+      strip_allreduce_store(a, tile_sum, col0, 0, kStripCols, 1, ll_epoch, 32 * (C + 1));
+      __syncthreads();
+      if (threadIdx.x == 0) ll_cta_done(a.ll, gridDim.x * gridDim.y);
+      return;
+    }
     for (int i = threadIdx.x; i < a.M * kStripCols; i += 32 * (C + 1)) {
       const int m = i / kStripCols, c = i % kStripCols;
       if (col0 + c < a.N) a.y[m * a.y_ld + col0 + c] = __float2half_rn(tile_sum[m * kStripCols + c]);
@@ -369,6 +427,18 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
   // K split across the CTAs of a cluster: CTA r sums column slice r of every
   // CTA's tile through distributed shared memory, in fixed rank order.
   cluster_sync();
+  if (fused) {
+    if (!failed && !ll_skip) {
+      // Pair-aligned column slices, so that every exchanged line is one CTA's.
+      const int S = a.ksplit;
+      const int c_lo = (static_cast<int>(blockIdx.y) * (kStripCols / 2)) / S * 2;
+      const int c_hi = ((static_cast<int>(blockIdx.y) + 1) * (kStripCols / 2)) / S * 2;
+      strip_allreduce_store(a, tile_sum, col0, c_lo, c_hi, S, ll_epoch, 32 * (C + 1));
+    }
+    cluster_sync();  // keep shared memory alive until every remote read is done
+    if (!failed && !ll_skip && threadIdx.x == 0) ll_cta_done(a.ll, gridDim.x * gridDim.y);
+    return;
+  }
   if (!failed) {
     const int S = a.ksplit;
     const int c_lo = (static_cast<int>(blockIdx.y) * kStripCols) / S;
@@ -492,13 +562,13 @@ bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p) {
   return true;
 }
 
-template <int MT, int C, bool RAW, bool PERM>
+template <int MT, int C, bool RAW, bool PERM, bool FUSED>
 int launch_strip_t(const StripMaps& maps, const StripArgs& args, int tiles, size_t smem, cudaStream_t stream) {
   const int ks = args.ksplit;
   static std::atomic<bool> configured[64];  // zero-initialised (static storage)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ASHQK_ERR_CUDA;
-  auto kernel = gemv_strip_kernel<MT, C, RAW, PERM>;
+  auto kernel = gemv_strip_kernel<MT, C, RAW, PERM, FUSED>;
   if (!configured[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
@@ -527,6 +597,23 @@ int launch_strip_t(const StripMaps& maps, const StripArgs& args, int tiles, size
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
+  if (FUSED) {
+    // A CTA waits for the same CTA of every peer: all CTAs of the grid must be
+    // resident at once, or a peer's CTA could queue behind CTAs that wait.
+    int resident = 0;
+    if (ks > 1) {
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) return ASHQK_ERR_CUDA;
+      resident = clusters * ks;
+    } else {
+      int per_sm = 0, sms = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 32 * (C + 1), smem) != cudaSuccess ||
+          cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return ASHQK_ERR_CUDA;
+      resident = per_sm * sms;
+    }
+    if (resident < tiles * ks) return ASHQK_ERR_UNSUPPORTED;
+  }
   if (cudaLaunchKernelEx(&cfg, kernel, maps, args) != cudaSuccess) return ASHQK_ERR_CUDA;
   return ASHQK_OK;
 }
@@ -550,9 +637,10 @@ bool perm_rows() {
 
 template <int MT, int C>
 int launch_strip(const StripMaps& maps, const StripArgs& args, int tiles, size_t smem, cudaStream_t stream) {
-  if (!raw_unpack()) return launch_strip_t<MT, C, false, false>(maps, args, tiles, smem, stream);
-  return perm_rows() ? launch_strip_t<MT, C, true, true>(maps, args, tiles, smem, stream)
-                     : launch_strip_t<MT, C, true, false>(maps, args, tiles, smem, stream);
+  if (args.ll.regions != nullptr) return launch_strip_t<MT, C, false, false, true>(maps, args, tiles, smem, stream);
+  if (!raw_unpack()) return launch_strip_t<MT, C, false, false, false>(maps, args, tiles, smem, stream);
+  return perm_rows() ? launch_strip_t<MT, C, true, true, false>(maps, args, tiles, smem, stream)
+                     : launch_strip_t<MT, C, true, false, false>(maps, args, tiles, smem, stream);
 }
 
 }  // namespace
@@ -563,9 +651,11 @@ bool gemv_strip_eligible(const void* x, int64_t x_ld, const int32_t* qw, int64_t
          qz_ld % 4 == 0 && aligned(s, 16) && s_ld % 8 == 0 && aligned(x, 16) && x_ld % 8 == 0;
 }
 
-int gemv_strip_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
+namespace {
+
+int strip_launch_impl(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
                       int64_t qz_ld, const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K, int G,
-                      int sm_count, cudaStream_t stream) {
+                      int sm_count, const LLPeers* ll, cudaStream_t stream) {
   StripPlan p;
   if (!plan_strip(M, N, K, G, sm_count, &p)) return ASHQK_ERR_UNSUPPORTED;
   StripMaps maps;
@@ -581,7 +671,8 @@ int gemv_strip_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t 
     rc = encode_tensor_map_2d(&maps.z, CU_TENSOR_MAP_DATA_TYPE_INT32, const_cast<int32_t*>(qz), N / 8, K / G,
                               static_cast<uint64_t>(qz_ld) * 4, kStripWords, p.gps, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  StripArgs a;
+  StripArgs a = {};
+  if (ll) a.ll = *ll;
   a.y = y;
   a.y_ld = y_ld;
   a.M = M;
@@ -606,7 +697,41 @@ int gemv_strip_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t 
                           : launch_strip<1, 8>(maps, a, p.tiles, p.smem, stream);
 }
 
+}  // namespace
+
+int gemv_strip_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
+                      int64_t qz_ld, const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K, int G,
+                      int sm_count, cudaStream_t stream) {
+  return strip_launch_impl(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G, sm_count, nullptr, stream);
+}
+
 }  // namespace ashqk
+
+extern "C" int ashqk_w4a16_gemv_allreduce(const void* x, int64_t x_ld, const int32_t* qweight, int64_t qw_ld,
+                                          const int32_t* qzeros, int64_t qz_ld, const void* scales, int64_t s_ld,
+                                          void* y, int64_t y_ld, int M, int N, int K, int group_size,
+                                          const void* regions_dev, int rank, int world, int64_t max_elems,
+                                          void* stream) {
+  int rc = ashqk::check_awq_args(x, x_ld, qweight, qw_ld, qzeros, qz_ld, scales, s_ld, y, y_ld, M, N, K, group_size);
+  if (rc) return rc;
+  size_t region = 0;
+  if (!regions_dev || world < 1 || world > ashqk::kLLMaxRanks || rank < 0 || rank >= world ||
+      ashqk_p2p_ll_region_bytes(max_elems, &region) || static_cast<int64_t>(M) * N > max_elems)
+    return ASHQK_ERR_INVALID_ARGUMENT;
+  if (!ashqk::gemv_strip_eligible(x, x_ld, qweight, qw_ld, qzeros, qz_ld, scales, s_ld, M, N, group_size))
+    return ASHQK_ERR_UNSUPPORTED;
+  ashqk::DeviceInfo info;
+  rc = ashqk::device_info(&info);
+  if (rc) return rc;
+  ashqk::LLPeers ll;
+  ll.regions = static_cast<unsigned char* const*>(regions_dev);
+  ll.rank = rank;
+  ll.world = world;
+  ll.inbox_pairs = max_elems / 2;
+  return ashqk::strip_launch_impl(static_cast<const __half*>(x), x_ld, qweight, qw_ld, qzeros, qz_ld,
+                                  static_cast<const __half*>(scales), s_ld, static_cast<__half*>(y), y_ld, M, N, K,
+                                  group_size, info.sm_count, &ll, static_cast<cudaStream_t>(stream));
+}
 
 extern "C" int ashqk_gemv_strip_plan(int M, int N, int K, int group_size, int sm_count, ashqk_strip_plan* plan) {
   if (!plan || M <= 0 || N <= 0 || K <= 0 || group_size <= 0 || N % 8 || K % group_size || sm_count < 0)

@@ -29,6 +29,7 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "ll_lines.cuh"
 #include "sm100.cuh"
 
 namespace ashqk {
@@ -113,107 +114,48 @@ __global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(const __hal
   }
 }
 
-// ---- low-latency variant: the flag travels with the data -----------------------
+// ---- low-latency variant: the epoch travels with the data --------------------
 //
-//   region of each rank (one cudaMalloc, shared by CUDA IPC):
-//     [0, 256)          one epoch counter per CTA of the grid (at most 64 CTAs)
-//     [256, ...)        inbox[parity][source rank][pair]: 8-byte lines
-//                       {two fp16 of the source's partial, epoch}
-//
-//   CTA b handles pairs [b * kLLPairsPerCta, ...). A call: epoch = ++counter[b];
-//   every thread stores each of its pairs, with the epoch in the same 64-bit
-//   store, into inbox[epoch & 1][rank][pair] of every peer (one NVLink write,
-//   no fence: the 8-byte store is single-copy atomic, so a reader that sees the
-//   epoch sees the data), then reads its own inbox line of every peer until it
-//   carries the epoch (bounded, local memory), and sums in rank order in fp32.
-//
-// A rank overwrites a line of parity e & 1 at epoch e + 2 only after its CTA b
-// has read, at epoch e + 1, lines that each peer's CTA b wrote at e + 1 --
-// which that peer did after its call e had completed -- so no line is
-// overwritten before it is read. Calls must keep one grid shape per element
-// range (the pair-to-CTA map is fixed), which a fixed kLLPairsPerCta gives.
+// Region layout and protocol: ll_lines.cuh. CTA b handles pairs
+// [b * kLLPairsPerCta, ...): pushes each of them to every peer as one 8-byte
+// line, then sums the peers' lines of the same pairs from its own inbox.
 constexpr int kLLThreads = 256;
 constexpr int kLLPairsPerThread = 2;
 constexpr int kLLPairsPerCta = kLLThreads * kLLPairsPerThread;
 constexpr int kLLMaxCtas = 64;
 
-__device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __global__ void __launch_bounds__(kLLThreads) allreduce_ll_kernel(const __half* in, __half* out, int npairs,
-                                                               unsigned char* const* regions, int rank, int world,
-                                                               long long inbox_pairs) {
+                                                               const LLPeers peers) {
   __shared__ unsigned int epoch_s;
   __shared__ int failed_s;
-  unsigned char* mine = regions[rank];
   pdl_launch_dependents();
-  pdl_wait();  // the partial is the previous kernel's output
+  pdl_wait();  // the partial is the previous kernel's output; the call counter is final
   if (threadIdx.x == 0) {
-    failed_s = (atomicOr(&g_device_errors, 0u) & kDevErrPeer) != 0;
-    if (!failed_s) epoch_s = atomicAdd(reinterpret_cast<unsigned int*>(mine) + blockIdx.x, 1u) + 1u;
+    failed_s = ll_sticky_failure();
+    epoch_s = ll_call_epoch(peers);
   }
   __syncthreads();
   if (failed_s) return;
   const unsigned int epoch = epoch_s;
-  const long long parity_base = static_cast<long long>(epoch & 1u) * kMaxRanks * inbox_pairs;
   const unsigned int* src = reinterpret_cast<const unsigned int*>(in);
-
   unsigned int own[kLLPairsPerThread];
   int pair[kLLPairsPerThread];
 #pragma unroll
   for (int u = 0; u < kLLPairsPerThread; ++u) {
     pair[u] = blockIdx.x * kLLPairsPerCta + u * kLLThreads + threadIdx.x;
     own[u] = pair[u] < npairs ? src[pair[u]] : 0u;
+    if (pair[u] < npairs) ll_push(peers, epoch, pair[u], own[u]);
   }
-  // Push: one 8-byte line per pair into every peer's inbox.
-  for (int q = 0; q < world; ++q) {
-    if (q == rank) continue;
-    unsigned long long* box = reinterpret_cast<unsigned long long*>(regions[q] + kHeaderBytes) + parity_base +
-                              static_cast<long long>(rank) * inbox_pairs;
-#pragma unroll
-    for (int u = 0; u < kLLPairsPerThread; ++u)
-      if (pair[u] < npairs)
-        st_volatile_u64(box + pair[u], (static_cast<unsigned long long>(epoch) << 32) | own[u]);
-  }
-  // Pull from the own inbox, sum in rank order.
-  const unsigned long long* inbox = reinterpret_cast<const unsigned long long*>(mine + kHeaderBytes) + parity_base;
   bool failed = false;
 #pragma unroll
   for (int u = 0; u < kLLPairsPerThread; ++u) {
     if (pair[u] >= npairs) continue;
-    float a0 = 0.f, a1 = 0.f;
-    for (int r = 0; r < world; ++r) {
-      unsigned int v = own[u];
-      if (r != rank && !failed) {
-        const unsigned long long* line = inbox + static_cast<long long>(r) * inbox_pairs + pair[u];
-        unsigned long long w = ld_volatile_u64(line);
-        if (static_cast<unsigned int>(w >> 32) != epoch) {
-          const long long t0 = clock64();
-          do {
-            if (clock64() - t0 > kWaitLimitCycles) {
-              failed = true;
-              raise_device_error(kDevErrPeer);
-              break;
-            }
-            __nanosleep(32);
-            w = ld_volatile_u64(line);
-          } while (static_cast<unsigned int>(w >> 32) != epoch);
-        }
-        v = static_cast<unsigned int>(w);
-      }
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&v));
-      a0 += f.x;
-      a1 += f.y;
-    }
+    const float2 v = ll_pull_sum(peers, epoch, pair[u], own[u], failed);
     if (failed) break;
-    reinterpret_cast<__half2*>(out)[pair[u]] = __floats2half2_rn(a0, a1);
+    reinterpret_cast<__half2*>(out)[pair[u]] = __floats2half2_rn(v.x, v.y);
   }
+  __syncthreads();
+  if (threadIdx.x == 0) ll_cta_done(peers, gridDim.x);
 }
 
 }  // namespace
@@ -223,7 +165,7 @@ extern "C" int ashqk_p2p_ll_region_bytes(int64_t max_elems, size_t* bytes) {
   if (!bytes || max_elems <= 0 || max_elems % 8 ||
       max_elems > static_cast<int64_t>(ashqk::kLLMaxCtas) * ashqk::kLLPairsPerCta * 2)
     return ASHQK_ERR_INVALID_ARGUMENT;
-  *bytes = ashqk::kHeaderBytes + 2ull * ashqk::kMaxRanks * static_cast<size_t>(max_elems / 2) * 8;
+  *bytes = ashqk::kLLHeaderBytes + 2ull * ashqk::kLLMaxRanks * static_cast<size_t>(max_elems / 2) * 8;
   return ASHQK_OK;
 }
 
@@ -244,9 +186,13 @@ extern "C" int ashqk_allreduce_f16_ll(const void* in, void* out, int64_t n, cons
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = ashqk::pdl_enabled() ? 1 : 0;
+  ashqk::LLPeers peers;
+  peers.regions = static_cast<unsigned char* const*>(regions_dev);
+  peers.rank = rank;
+  peers.world = world;
+  peers.inbox_pairs = static_cast<long long>(max_elems / 2);
   if (cudaLaunchKernelEx(&cfg, ashqk::allreduce_ll_kernel, static_cast<const __half*>(in), static_cast<__half*>(out),
-                         npairs, static_cast<unsigned char* const*>(regions_dev), rank, world,
-                         static_cast<long long>(max_elems / 2)) != cudaSuccess)
+                         npairs, peers) != cudaSuccess)
     return ASHQK_ERR_CUDA;
   return ASHQK_OK;
 }

@@ -236,13 +236,33 @@ ASHQK_API int ashqk_allreduce_f16_oneshot(const void* in, void* out, int64_t n, 
  * call's epoch (no fence, no peer-load round trip) and polls its own region;
  * one CTA per 1024 elements (at most 64 CTAs). Regions are sized by
  * ashqk_p2p_ll_region_bytes (max_elems <= 65536) and set up exactly as for
- * ashqk_allreduce_f16_oneshot (allocate, export, import, pointer array); a
- * region serves one of the two variants. Same sum (fp32, rank order, one
- * rounding), same ~2 s peer limit and sticky device error bit 3.
+ * ashqk_allreduce_f16_oneshot (allocate, export, import, pointer array); an
+ * LL region serves this call and ashqk_w4a16_gemv_allreduce, not the one-shot
+ * call. Same sum (fp32, rank order, one rounding), same ~2 s peer limit and
+ * sticky device error bit 3.
  */
 ASHQK_API int ashqk_p2p_ll_region_bytes(int64_t max_elems, size_t* bytes);
 ASHQK_API int ashqk_allreduce_f16_ll(const void* in, void* out, int64_t n, const void* regions_dev, int rank,
                                      int world, int64_t max_elems, void* stream);
+
+/*
+ * Row-parallel decode layer with the all-reduce fused into the GEMV: every rank
+ * passes its K shard (x columns, qweight / qzeros / scales rows on group
+ * boundaries) and gets in y the sum over the ranks of the fp16 partials, in
+ * fp32, rank order, rounded once -- bit for bit what ashqk_w4a16_gemv followed
+ * by ashqk_allreduce_f16_ll gives. The partial never reaches HBM: the
+ * column-strip GEMV's epilogue pushes it to the peers as low-latency lines and
+ * sums theirs. Regions as for ashqk_allreduce_f16_ll (the two share a region
+ * and its call counter); M * N <= max_elems. Returns ASHQK_ERR_UNSUPPORTED
+ * (nothing launched) when the column-strip kernel does not take the problem
+ * or cannot keep its whole grid resident; the caller then runs the two steps.
+ * No reference counterpart: the reference has no multi-GPU code.
+ */
+ASHQK_API int ashqk_w4a16_gemv_allreduce(const void* x, int64_t x_ld, const int32_t* qweight, int64_t qw_ld,
+                                         const int32_t* qzeros, int64_t qz_ld, const void* scales, int64_t s_ld,
+                                         void* y, int64_t y_ld, int M, int N, int K, int group_size,
+                                         const void* regions_dev, int rank, int world, int64_t max_elems,
+                                         void* stream);
 
 #ifdef __cplusplus
 }

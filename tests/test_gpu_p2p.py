@@ -191,26 +191,18 @@ def test_ll_protocol_and_sum(lib):
     regs = _LLRegions(lib, 1 << 15)
     g = torch.Generator(device="cuda")
     g.manual_seed(1)
-    for epoch, shape in enumerate([(4, 4096), (1, 4096), (8, 4096), (2, 8)], start=1):
+    for e, shape in enumerate([(4, 4096), (1, 4096), (8, 4096), (2, 8)], start=1):
         n = shape[0] * shape[1]
-        ctas = -(-(n // 2) // 512)
         a = (torch.randn(shape, device="cuda", generator=g) * 2).half()
         b = (torch.randn(shape, device="cuda", generator=g) * 2).half()
-        # Every CTA keeps its own epoch (calls of different sizes run different CTA counts): the
-        # pairs of CTA c travel with epoch counters[c] + 1 in slot parity (counters[c] + 1) & 1.
-        ep = [int(v) + 1 for v in regs.counters(0)[:ctas].tolist()]
-        pa, pb = _pack_lines(a, 0), _pack_lines(b, 0)
-        for c, e in enumerate(ep):
-            sl = slice(512 * c, min(512 * (c + 1), n // 2))
-            regs.lines(0, e & 1, 1)[sl] = pb[sl] | (e << 32)             # the peer's pushed lines
+        assert regs.counters(0)[:2].tolist() == [e - 1, 0]               # calls done, CTAs finished
+        regs.lines(0, e & 1, 1)[: n // 2] = _pack_lines(b, e)            # the peer's pushed lines
         out = torch.full_like(a, float("nan"))
         assert _call_ll(lib, regs, a, out) == 0
         torch.cuda.synchronize()
-        assert torch.equal(out, (a.float() + b.float()).half()), epoch
-        assert regs.counters(0)[:ctas].tolist() == ep
-        for c, e in enumerate(ep):                                       # pushed to the peer
-            sl = slice(512 * c, min(512 * (c + 1), n // 2))
-            assert torch.equal(regs.lines(1, e & 1, 0)[sl], pa[sl] | (e << 32)), (epoch, c)
+        assert torch.equal(out, (a.float() + b.float()).half()), e
+        assert regs.counters(0)[:2].tolist() == [e, 0]                   # the last CTA bumped it
+        assert torch.equal(regs.lines(1, e & 1, 0)[: n // 2], _pack_lines(a, e))  # pushed to the peer
     a = torch.randn(8, 512, device="cuda", generator=g).half()
     ref = a.clone()
     assert _call_ll(lib, regs, a, a, world=1) == 0                       # world 1: a copy, in place
@@ -234,6 +226,58 @@ def test_ll_missing_peer_times_out(lib):
         t0 = time.time()
         assert _call_ll(lib, regs, a, out) == 0                           # sticky: returns at once
         torch.cuda.synchronize()
-        assert time.time() - t0 < 0.5 and int(regs.counters(0)[0]) == 1
+        assert time.time() - t0 < 0.5 and regs.counters(0)[:2].tolist() == [1, 0]
     finally:
         _errors(lib, clear=True)
+
+
+def _fused_call(lib, regs, x, qw, qz, s, y, rank=0, world=2):
+    vp, i64, ci = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    lib.ashqk_w4a16_gemv_allreduce.argtypes = [vp, i64, vp, i64, vp, i64, vp, i64, vp, i64, ci, ci, ci, ci, vp, ci,
+                                               ci, i64, vp]
+    m, k = x.shape
+    n = qw.shape[1] * 8
+    return lib.ashqk_w4a16_gemv_allreduce(x.data_ptr(), x.stride(0), qw.data_ptr(), qw.stride(0), qz.data_ptr(),
+                                          qz.stride(0), s.data_ptr(), s.stride(0), y.data_ptr(), y.stride(0), m, n, k,
+                                          k // s.shape[0], regs.ptrs.data_ptr(), rank, world, regs.max_elems,
+                                          torch.cuda.current_stream().cuda_stream)
+
+
+@ll_pending
+@pytest.mark.parametrize("m,n,k", [(1, 4096, 2048), (4, 4096, 6144), (16, 4096, 512), (2, 96, 1024)])
+def test_fused_row_parallel_gemv(lib, m, n, k):
+    """Rank 0 of two with the host playing rank 1: the fused kernel's y equals the unfused GEMV's
+    fp16 partial plus rank 1's, summed in fp32 and rounded once; the lines it pushed carry its
+    partial; the region's call counter advances once per call (shared with the LL all-reduce)."""
+    import ashqk
+    from tests._helpers import quantized_problem, to_cuda
+
+    _errors(lib, clear=True)
+    regs = _LLRegions(lib, 1 << 16)
+    x0, qw0, qz0, s0 = to_cuda(*quantized_problem(m, n, k, 128, seed=m + 1))
+    x1, qw1, qz1, s1 = to_cuda(*quantized_problem(m, n, k, 128, seed=m + 101))
+    y0 = ashqk.w4a16_linear(x0, qw0, qz0, s0)   # this rank's partial, as the unfused GEMV stores it
+    y1 = ashqk.w4a16_linear(x1, qw1, qz1, s1)   # the peer's
+    for e in (1, 2, 3):
+        regs.lines(0, e & 1, 1)[: m * n // 2] = _pack_lines(y1, e)
+        y = torch.full((m, n), float("nan"), dtype=torch.float16, device="cuda")
+        assert _fused_call(lib, regs, x0, qw0, qz0, s0, y) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(y, (y0.float() + y1.float()).half()), (m, n, k, e)
+        assert torch.equal(regs.lines(1, e & 1, 0)[: m * n // 2], _pack_lines(y0, e))
+        assert regs.counters(0)[:2].tolist() == [e, 0]
+    assert _errors(lib) == 0
+
+
+@ll_pending
+def test_fused_declines_what_it_cannot_take(lib):
+    regs = _LLRegions(lib, 1 << 12)
+    x = torch.zeros(2, 1024, dtype=torch.float16, device="cuda")
+    qw = torch.zeros(1024, 4096 // 8, dtype=torch.int32, device="cuda")
+    qz = torch.zeros(8, 4096 // 8, dtype=torch.int32, device="cuda")
+    s = torch.ones(8, 4096, dtype=torch.float16, device="cuda")
+    y = torch.empty(2, 4096, dtype=torch.float16, device="cuda")
+    assert _fused_call(lib, regs, x, qw, qz, s, y) == 1               # M * N > max_elems
+    regs = _LLRegions(lib, 1 << 16)
+    assert _fused_call(lib, regs, x[:, :1024], qw[:, :5], qz[:, :5], s[:, :40], y[:, :40]) == 2  # N % 32
+    assert regs.counters(0)[:2].tolist() == [0, 0]                     # nothing launched

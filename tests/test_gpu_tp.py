@@ -206,6 +206,10 @@ def _p2p_worker(rank, world, port, protocol="oneshot"):
         y_p2p = tp.row_parallel_linear(xs, *sh, allreduce=ar)
         y_nccl = tp.row_parallel_linear(xs, *sh, reduce_dtype=torch.float32)
         assert float((y_p2p.float() - y_nccl.float()).abs().max()) <= 1e-2 * float(y_nccl.float().abs().max())
+        if protocol == "ll":  # the fused GEMV + all-reduce equals the two steps bit for bit
+            from ashqk import w4a16_linear
+
+            assert torch.equal(y_p2p, ar(w4a16_linear(xs, *sh)))
         ar.check()
         ar.close()
         dist.barrier()

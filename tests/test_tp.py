@@ -81,6 +81,7 @@ class _FakeP2PLib:
         self.ashqk_p2p_region_bytes, self.ashqk_p2p_alloc, self.ashqk_p2p_export = region_bytes, alloc, export
         self.ashqk_p2p_import, self.ashqk_p2p_close, self.ashqk_p2p_free = import_, close, free
         self.ashqk_allreduce_f16_oneshot = self.ashqk_allreduce_f16_ll = nop
+        self.ashqk_w4a16_gemv_allreduce = lambda *args: 0
         self.ashqk_p2p_ll_region_bytes = region_bytes
         self.ashqk_get_device_errors = nop
 
