@@ -408,16 +408,18 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
     ll_skip = ll_sticky_failure();
     ll_epoch = ll_call_epoch(a.ll);
   }
+  // A fused call counts every CTA as done, even one whose pipeline gave up,
+  // so that the region's call counter stays in step with the peers'.
   if (a.ksplit == 1) {
     __syncthreads();
-    if (failed) return;
     if (fused) {
       if (ll_skip) return;
-      strip_allreduce_store(a, tile_sum, col0, 0, kStripCols, 1, ll_epoch, 32 * (C + 1));
+      if (!failed) strip_allreduce_store(a, tile_sum, col0, 0, kStripCols, 1, ll_epoch, 32 * (C + 1));
       __syncthreads();
       if (threadIdx.x == 0) ll_cta_done(a.ll, gridDim.x * gridDim.y);
       return;
     }
+    if (failed) return;
     for (int i = threadIdx.x; i < a.M * kStripCols; i += 32 * (C + 1)) {
       const int m = i / kStripCols, c = i % kStripCols;
       if (col0 + c < a.N) a.y[m * a.y_ld + col0 + c] = __float2half_rn(tile_sum[m * kStripCols + c]);
@@ -436,7 +438,7 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
       strip_allreduce_store(a, tile_sum, col0, c_lo, c_hi, S, ll_epoch, 32 * (C + 1));
     }
     cluster_sync();  // keep shared memory alive until every remote read is done
-    if (!failed && !ll_skip && threadIdx.x == 0) ll_cta_done(a.ll, gridDim.x * gridDim.y);
+    if (!ll_skip && threadIdx.x == 0) ll_cta_done(a.ll, gridDim.x * gridDim.y);
     return;
   }
   if (!failed) {
