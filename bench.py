@@ -238,31 +238,36 @@ def make_stack(world, rank, device, n_layers=N_LAYERS):
     return stack
 
 
-def stack_step(stack, h, world, group, allreduce=None):
+def stack_step(stack, h, world, group, allreduce=None, fused=False):
     """One token through every linear layer (public API calls). The row-parallel partials are summed
-    with NCCL, or with ``allreduce`` (an ``ashqk.tp.P2PAllReduce``) when given."""
+    with NCCL, or with ``allreduce`` (an ``ashqk.tp.P2PAllReduce``) when given; with ``fused`` the
+    row-parallel layers run as one GEMV + all-reduce kernel each where it takes them."""
     import torch.distributed as dist
 
     from ashqk import w4a16_linear
 
-    def reduce(t):
+    def row_parallel(x, weights):
+        if world > 1 and fused:
+            y = allreduce.fused_linear(x, *weights)
+            if y is not None:
+                return y
+        y = w4a16_linear(x, *weights)                           # partial [M, 4096]
         if world > 1:
             if allreduce is not None:
-                allreduce(t, out=t)
+                allreduce(y, out=y)
             else:
-                dist.all_reduce(t, group=group)
+                dist.all_reduce(y, group=group)
+        return y
 
     out = None
     for layer in stack:
         a = w4a16_linear(h, *layer["qkv"])                      # [M, 6144/P]
         # Attention output stands in as the first columns of qkv (o input: 4096/P per rank).
         o_in = a[:, : 4096 // world]
-        b = w4a16_linear(o_in, *layer["o"])                     # partial [M, 4096]
-        reduce(b)
+        b = row_parallel(o_in, layer["o"])                      # [M, 4096], summed over ranks
         c = w4a16_linear(b, *layer["gate_up"])                  # [M, 24576/P]
         d_in = c[:, : 12288 // world]
-        out = w4a16_linear(d_in, *layer["down"])                # partial [M, 4096]
-        reduce(out)
+        out = row_parallel(d_in, layer["down"])                 # [M, 4096], summed over ranks
     return out
 
 
@@ -593,23 +598,25 @@ def run_gpu(args):
             print(json.dumps({"prefill": res}), flush=True)
         return
     stack = make_stack(world, rank, device, args.layers)
-    # Tensor-parallel reductions: NCCL by default, the NVLink kernels with
-    # ASHQK_TP_ALLREDUCE=p2p (one-shot) or =ll (low-latency lines).
+    # Tensor-parallel reductions: NCCL by default; the NVLink kernels with
+    # ASHQK_TP_ALLREDUCE=p2p (one-shot), =ll (low-latency lines) or =fused (the
+    # row-parallel GEMV and its all-reduce as one kernel, low-latency lines).
     p2p = None
     tp_reduce = os.environ.get("ASHQK_TP_ALLREDUCE", "nccl")
-    if world > 1 and tp_reduce in ("p2p", "ll"):
+    fused = world > 1 and tp_reduce == "fused"
+    if world > 1 and tp_reduce in ("p2p", "ll", "fused"):
         from ashqk import tp
 
-        p2p = tp.P2PAllReduce(group=group, max_elems=4 * 4096, protocol="ll" if tp_reduce == "ll" else "oneshot")
+        p2p = tp.P2PAllReduce(group=group, max_elems=4 * 4096, protocol="oneshot" if tp_reduce == "p2p" else "ll")
     results = {}
     graphs = {}
     for m in (1, 4):
         h = torch.randn(m, 4096, device=device).half()
-        stack_step(stack, h, world, group, p2p)  # warm-up outside capture (workspaces, NCCL comms)
+        stack_step(stack, h, world, group, p2p, fused)  # warm-up outside capture (workspaces, NCCL comms)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            out = stack_step(stack, h, world, group, p2p)
+            out = stack_step(stack, h, world, group, p2p, fused)
         graphs[m] = (g, h, out)
         del g  # the dict holds the only reference (graphs with NCCL calls must be freed before teardown)
 
