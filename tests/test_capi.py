@@ -160,3 +160,27 @@ def test_strip_plan_of_the_measured_layers(lib):
     for (n, k), (gx, gy, threads) in want.items():
         rc, p = _strip_plan(lib, 1, n, k, 128, 148)
         assert rc == 0 and (p.grid_x, p.grid_y, p.threads) == (gx, gy, threads), (n, k, p.grid_x, p.grid_y, p.threads)
+
+
+def test_fused_epilogue_covers_every_pair_once(lib):
+    """The fused row-parallel epilogue: CTA (strip, r) of a K-split cluster of S exchanges the pairs
+    of columns [((r * 32) // S) * 2, (((r + 1) * 32) // S) * 2) of its 64-column strip, for every
+    token. Over the planner's grids for the tensor-parallel decode shards, the CTAs' pairs cover
+    y [M, N] exactly once and every line index lies inside the inbox of M * N / 2 pairs."""
+    for n, k in [(4096, 2048), (4096, 6144), (4096, 512), (4096, 1024), (8192, 3584), (96, 1024)]:
+        for m in (1, 4, 16):
+            rc, p = _strip_plan(lib, m, n, k, 128, 148)
+            assert rc == 0
+            seen = {}
+            for strip in range(p.grid_x):
+                for r in range(p.grid_y):
+                    lo, hi = (r * 32) // p.grid_y * 2, ((r + 1) * 32) // p.grid_y * 2
+                    for tok in range(m):
+                        for c in range(lo, hi, 2):
+                            col = strip * 64 + c
+                            if col >= n:
+                                continue
+                            pair = tok * (n // 2) + col // 2
+                            assert pair not in seen, (n, k, m, strip, r, c)
+                            seen[pair] = (strip, r)
+            assert sorted(seen) == list(range(m * n // 2)), (n, k, m)
