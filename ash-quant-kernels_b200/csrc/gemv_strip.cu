@@ -720,7 +720,9 @@ extern "C" int ashqk_w4a16_gemv_allreduce(const void* x, int64_t x_ld, const int
   if (!regions_dev || world < 1 || world > ashqk::kLLMaxRanks || rank < 0 || rank >= world ||
       ashqk_p2p_ll_region_bytes(max_elems, &region) || static_cast<int64_t>(M) * N > max_elems)
     return ASHQK_ERR_INVALID_ARGUMENT;
-  if (!ashqk::gemv_strip_eligible(x, x_ld, qweight, qw_ld, qzeros, qz_ld, scales, s_ld, M, N, group_size))
+  // The epilogue stores y as fp16 pairs.
+  if (!ashqk::gemv_strip_eligible(x, x_ld, qweight, qw_ld, qzeros, qz_ld, scales, s_ld, M, N, group_size) ||
+      !ashqk::aligned(y, 4) || y_ld % 2)
     return ASHQK_ERR_UNSUPPORTED;
   ashqk::DeviceInfo info;
   rc = ashqk::device_info(&info);
