@@ -184,3 +184,38 @@ def test_fused_epilogue_covers_every_pair_once(lib):
                             assert pair not in seen, (n, k, m, strip, r, c)
                             seen[pair] = (strip, r)
             assert sorted(seen) == list(range(m * n // 2)), (n, k, m)
+
+
+def test_p2p_entry_points_validate_before_the_device(lib):
+    """The NVLink all-reduce and fused row-parallel entry points refuse malformed calls before any
+    CUDA call (fake pointers are never dereferenced); a well-formed fused call needs the device."""
+    vp, i64, ci = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    fake, regions = ctypes.c_void_p(0x10000), ctypes.c_void_p(0x20000)
+    size = ctypes.c_size_t(0)
+    lib.ashqk_p2p_region_bytes.argtypes = [i64, ctypes.POINTER(ctypes.c_size_t)]
+    lib.ashqk_p2p_ll_region_bytes.argtypes = [i64, ctypes.POINTER(ctypes.c_size_t)]
+    assert lib.ashqk_p2p_region_bytes(12, ctypes.byref(size)) == 1            # not a multiple of 8
+    assert lib.ashqk_p2p_ll_region_bytes(1 << 17, ctypes.byref(size)) == 1    # above 65536
+    assert lib.ashqk_p2p_ll_region_bytes(1 << 16, ctypes.byref(size)) == 0
+    assert size.value == 256 + 2 * 8 * (1 << 15) * 8
+    for name in ("ashqk_allreduce_f16_oneshot", "ashqk_allreduce_f16_ll"):
+        f = getattr(lib, name)
+        f.argtypes = [vp, vp, i64, vp, ci, ci, i64, vp]
+        assert f(fake, fake, 1024, None, 0, 2, 4096, None) == 1               # no region array
+        assert f(fake, fake, 1020, regions, 0, 2, 4096, None) == 1            # n % 8
+        assert f(fake, fake, 8192, regions, 0, 2, 4096, None) == 1            # n > max_elems
+        assert f(fake, fake, 1024, regions, 2, 2, 4096, None) == 1            # rank outside world
+        assert f(fake, fake, 1024, regions, 0, 9, 4096, None) == 1            # more than 8 ranks
+        assert f(ctypes.c_void_p(0x10002), fake, 1024, regions, 0, 2, 4096, None) == 1  # misaligned
+    g = lib.ashqk_w4a16_gemv_allreduce
+    g.argtypes = [vp, i64, vp, i64, vp, i64, vp, i64, vp, i64, ci, ci, ci, ci, vp, ci, ci, i64, vp]
+    ok = (fake, 2048, fake, 512, fake, 512, fake, 4096, fake, 4096, 1, 4096, 2048, 128)
+    assert g(*ok, None, 0, 2, 1 << 16, None) == 1                             # no region array
+    assert g(*ok, regions, 0, 2, 2048, None) == 1                             # M * N > max_elems
+    assert g(*ok, regions, 3, 2, 1 << 16, None) == 1                          # rank outside world
+    bad_n = (fake, 2048, fake, 5, fake, 5, fake, 40, fake, 40, 1, 40, 2048, 128)
+    assert g(*bad_n, regions, 0, 2, 1 << 16, None) == 2                       # N % 32: not the strip kernel
+    import torch
+
+    if not torch.cuda.is_available():
+        assert g(*ok, regions, 0, 2, 1 << 16, None) == 5                      # needs the device's SM count
