@@ -219,3 +219,20 @@ def test_p2p_entry_points_validate_before_the_device(lib):
 
     if not torch.cuda.is_available():
         assert g(*ok, regions, 0, 2, 1 << 16, None) == 5                      # needs the device's SM count
+
+
+@pytest.mark.parametrize("lang,std", [("c", "-std=c99"), ("c++", "-std=c++11")])
+def test_header_compiles_standalone(lang, std, tmp_path):
+    """The C ABI header is self-contained plain C (and valid C++): no CUDA or torch headers needed."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc" if lang == "c" else "g++")
+    if cc is None:
+        pytest.skip("no host compiler")
+    src = tmp_path / ("use." + ("c" if lang == "c" else "cpp"))
+    src.write_text('#include "ashqk_b200.h"\nint main(void) { ashqk_strip_plan p; (void)p; '
+                   'return ashqk_version() == 0; }\n')
+    r = subprocess.run([cc, std, "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-I", os.path.dirname(HEADER),
+                        str(src)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
