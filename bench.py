@@ -317,9 +317,28 @@ def per_layer_gemv(stack, m, torch, reps=3):
         torch.cuda.synchronize()
         us = start.elapsed_time(end) * 1e3 / (reps * len(stack))
         nbytes = w4a16_bytes(m, n, k, GROUP)
-        res[name] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1)}
+        res[name] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1), "launch": strip_plan(m, n, k)}
         del g
     return res
+
+
+def strip_plan(m, n, k):
+    """The column-strip GEMV's launch shape for this layer on this device (ashqk_gemv_strip_plan)."""
+    import ctypes
+
+    from ashqk import _ext
+
+    class Plan(ctypes.Structure):
+        _fields_ = [(f, ctypes.c_int) for f in ("grid_x", "grid_y", "threads", "consumer_warps", "ring_stages",
+                                                "stages_total", "stage_bytes", "smem_bytes")]
+
+    lib = ctypes.CDLL(_ext.C_LIBRARY)
+    lib.ashqk_gemv_strip_plan.argtypes = [ctypes.c_int] * 5 + [ctypes.POINTER(Plan)]
+    p = Plan()
+    if lib.ashqk_gemv_strip_plan(m, n, k, GROUP, 0, ctypes.byref(p)) != 0:
+        return None
+    return {"grid": [p.grid_x, p.grid_y], "threads": p.threads, "ring_stages": p.ring_stages,
+            "smem_kb": round(p.smem_bytes / 1024, 1)}
 
 
 def cublas_fp16_stack(stack, steps, warmup, torch):
