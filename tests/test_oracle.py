@@ -102,3 +102,37 @@ def test_bytes_model():
     # bench/bench_gemm.py:45-46 of the reference; qkv M=1 is 13.10 MB.
     assert O.w4a16_bytes(1, 6144, 4096, 128) == 1 * 4096 * 2 + 4096 * 6144 // 2 + 32 * 6144 * 2 + 32 * 6144 // 2 + 6144 * 2
     assert abs(O.w4a16_bytes(1, 6144, 4096, 128) / 1e6 - 13.10) < 0.01
+
+
+@pytest.mark.parametrize("mutation", ["sequential_nibbles", "zero_point_off_by_one", "scale_of_next_group",
+                                      "fp16_accumulation"])
+def test_criterion_catches_planted_mistakes(golden, mutation):
+    """The parity criterion has teeth: products computed with a planted mistake (in the oracle,
+    on the CPU) fail it. The reference records the first of these by hand: sequential nibble
+    order gives rel err 1.24 (results/v0.1-naive-findings.md:8)."""
+    name = _cases(golden)[0]
+    x, qw, qz, s = (golden[f"{name}_{k}"] for k in ("x", "qweight", "qzeros", "scales"))
+    y_true = O.c_gemm(x, qw, qz, s)
+    e_fp16 = O.rel_err(golden[f"{name}_y_ref"], y_true)
+    k, g = qw.shape[0], qw.shape[0] // s.shape[0]
+    q = O.unpack_awq(qw).astype(np.float32)
+    z = O.unpack_awq(qz).astype(np.float32)
+    if mutation == "sequential_nibbles":  # nibble i read as column i instead of AWQ_ORDER[i]
+        w8 = qw.view(np.uint32)
+        q = np.stack([(w8 >> np.uint32(4 * i)) & np.uint32(15) for i in range(8)], -1).reshape(k, -1)
+        q = q.astype(np.float32)
+    elif mutation == "zero_point_off_by_one":
+        z = z + 1
+    zs = np.repeat(z, g, axis=0)
+    ss = np.repeat(s.astype(np.float32), g, axis=0)
+    if mutation == "scale_of_next_group":
+        ss = np.repeat(np.roll(s.astype(np.float32), -1, axis=0), g, axis=0)
+    w = ((q - zs) * ss).astype(np.float16).astype(np.float32)
+    if mutation == "fp16_accumulation":  # every partial sum rounded to fp16
+        acc = np.zeros((x.shape[0], w.shape[1]), np.float16)
+        for kk in range(k):
+            acc = (acc + (x[:, kk:kk + 1].astype(np.float32) * w[kk]).astype(np.float16)).astype(np.float16)
+        y = acc.astype(np.float32)
+    else:
+        y = x.astype(np.float32) @ w
+    assert O.rel_err(y, y_true) > 2 * e_fp16 + 1e-5, (mutation, O.rel_err(y, y_true), e_fp16)
