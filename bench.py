@@ -707,6 +707,8 @@ def run_gpu(args):
         "stack_hbm_frac": round(stack_gbs / hbm_peak, 3),
         "gpu_launches": args.steps * len(LAYERS) * n_layers,
         "clocks": clocks.summary(),
+        "device": {"name": torch.cuda.get_device_name(device),
+                   "sm_count": torch.cuda.get_device_properties(device).multi_processor_count},
         "e2e": {"value": round(e2e_ms * 1e3, 1), "unit": UNIT, "h2d_bytes_per_step": 4096 * 2,
                 "d2h_bytes_per_step": d2h_bytes,
                 "how": f"pinned H2D of the token's hidden state + CUDA-graph replay of the "
