@@ -622,6 +622,8 @@ def run_gpu(args):
     # row-parallel GEMV and its all-reduce as one kernel, low-latency lines).
     p2p = None
     tp_reduce = os.environ.get("ASHQK_TP_ALLREDUCE", "nccl")
+    if tp_reduce not in ("nccl", "p2p", "ll", "fused"):
+        raise SystemExit(f"ASHQK_TP_ALLREDUCE={tp_reduce!r}: expected nccl, p2p, ll or fused")
     fused = world > 1 and tp_reduce == "fused"
     if world > 1 and tp_reduce in ("p2p", "ll", "fused"):
         from ashqk import tp
