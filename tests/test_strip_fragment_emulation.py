@@ -186,3 +186,95 @@ def test_raw_flush_recovers_q_minus_z(perm):
                     ks = slice(16 * s, 16 * s + 16)
                     want = float(xf[tok, ks] @ (q[ks, col] - z[0, col]))
                     assert got == pytest.approx(want, rel=1e-9, abs=1e-6), (perm, s, lane, j, c)
+
+
+def _consumer_strip(x, q, z, s_scales, g_size, raw, perm):
+    """The consumer warp's whole K loop for one 64-column strip, lane by lane: per 16-row step the
+    warp-wide mma on the assembled fragments (fp32 accumulation into the lanes' partials), a flush
+    at every quantization-group change (RAW: the per-group correction), and the final per-lane
+    accumulators mapped back to y[token, column] as the kernel's reduction stores them."""
+    m, k = x.shape
+    mt_count = 2 if m > 8 else 1
+    words = O.pack_awq(q.astype(np.int32)).view(np.uint32)          # [K, 8]
+    zwords = O.pack_awq(z.astype(np.int32)).view(np.uint32)         # [K/G, 8]
+    low = np.array([c % 4 < 2 for c in range(8)])
+    acc = np.zeros((32, mt_count, 4, 4), np.float32)
+    part = np.zeros_like(acc)
+    psx = np.zeros((32, mt_count, 4), np.float32)
+    cur = -1
+    for k0 in range(0, k, 256):
+        stage = Stage(words[k0:k0 + 256], x[:, k0:k0 + 256])
+        if perm:
+            stage.x_prep()
+        for s in range(min(256, k - k0) // 16):
+            grp = (k0 + 16 * s) // g_size
+            if grp != cur:
+                if cur >= 0:
+                    _flush(acc, part, psx, zwords[cur], s_scales[cur], raw)
+                cur = grp
+            A, B = emulate_step(stage, s, perm, mt_count)
+            if not raw:  # the subtracting variant feeds (q - z): rebuild A from the magic values
+                zc = z[cur]
+                for j in range(4):
+                    for r in range(16):
+                        col = 8 * (r % 8) + j + (4 if r >= 8 else 0)
+                        A[j, r] = (A[j, r] - 1024) / (1 if low[col % 8] else 16) - zc[col]
+            for lane in range(32):
+                g, t = lane >> 2, lane & 3
+                for mt in range(mt_count):
+                    for j in range(4):
+                        C = (A[j].astype(np.float64) @ B[mt].astype(np.float64)).astype(np.float32)
+                        part[lane, mt, j] += np.array([C[g, 2 * t], C[g, 2 * t + 1], C[g + 8, 2 * t],
+                                                       C[g + 8, 2 * t + 1]], np.float32)
+                    sx = B[mt].sum(axis=0).astype(np.float32)           # the ones-mma, column n
+                    psx[lane, mt] += np.array([sx[2 * t], sx[2 * t + 1], 0, 0], np.float32)
+    _flush(acc, part, psx, zwords[cur], s_scales[cur], raw)
+    y = np.zeros((m, 64), np.float32)
+    for lane in range(32):
+        g, t = lane >> 2, lane & 3
+        for mt in range(mt_count):
+            for j in range(4):
+                for e, (dc, dt) in enumerate([(0, 0), (0, 1), (4, 0), (4, 1)]):
+                    tok = 8 * mt + 2 * t + dt
+                    if tok < m:
+                        y[tok, 8 * g + j + dc] = acc[lane, mt, j, e]
+    return y
+
+
+def _flush(acc, part, psx, zrow_words, srow, raw):
+    for lane in range(32):
+        g = lane >> 2
+        zw = int(zrow_words[g])
+        zk = [((zw >> (4 * NIBBLE_OF_COL[c])) & 15) + (64.0 if c & 2 else 1024.0) for c in range(8)]
+        sc = srow[8 * g:8 * g + 8].astype(np.float32)
+        for mt in range(part.shape[1]):
+            for j in range(4):
+                p = part[lane, mt, j].copy()
+                if raw:
+                    f = np.float32(1.0 if j < 2 else 1 / 16)
+                    p = p * f - np.array([zk[j] * psx[lane, mt, 0], zk[j] * psx[lane, mt, 1],
+                                          zk[4 + j] * psx[lane, mt, 0], zk[4 + j] * psx[lane, mt, 1]], np.float32)
+                acc[lane, mt, j] += np.array([sc[j], sc[j], sc[4 + j], sc[4 + j]], np.float32) * p
+                part[lane, mt, j] = 0
+            psx[lane, mt] = 0
+
+
+@pytest.mark.parametrize("g_size", [32, 64, 128])
+@pytest.mark.parametrize("m", [1, 9])
+@pytest.mark.parametrize("raw,perm", [(False, False), (True, False), (True, True)])
+def test_consumer_loop_matches_the_oracle(g_size, m, raw, perm):
+    """The strip consumer's K loop (two stages, several quantization groups) in each variant gives
+    y within the reference's parity criterion of the oracle's fp64 truth, on one 64-column strip."""
+    rng = np.random.default_rng(g_size + 7 * m)
+    k = 512
+    q = rng.integers(0, 16, (k, 64))
+    z = rng.integers(0, 16, (k // g_size, 64))
+    s_scales = (rng.random((k // g_size, 64)) * 0.018 + 0.002).astype(np.float16)
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    qw, qz = O.pack_awq(q.astype(np.int32)), O.pack_awq(z.astype(np.int32))
+    y_true = O.w4a16_gemm_fp64(x, qw, qz, s_scales)
+    w16 = O.dequantize_awq(qw, qz, s_scales, np.float16)
+    e_fp16 = O.rel_err((x.astype(np.float32) @ w16.astype(np.float32)).astype(np.float16).astype(np.float32),
+                       y_true)
+    y = _consumer_strip(x, q, z, s_scales, g_size, raw, perm).astype(np.float16).astype(np.float32)
+    assert O.rel_err(y, y_true) <= 2 * e_fp16 + 1e-5, (O.rel_err(y, y_true), e_fp16)
