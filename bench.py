@@ -546,10 +546,12 @@ def marlin_compare(torch, reps=3):
     return res
 
 
-def tp_mlp(world, rank, group, reps, warmup, torch, dist):
+def tp_mlp(world, rank, group, reps, warmup, torch, dist, hbm_peak, tensor_peak):
     """a large dense MLP under tensor parallelism (gate_up K=8192 N=57344
     column-parallel + NCCL all-gather; down K=28672 N=8192 row-parallel + all-reduce), per M:
-    device time of the two layers with their collectives, max over ranks."""
+    device time of the two layers with their collectives, max over ranks, and the fraction of the
+    per-rank roofline -- HBM (algorithmic bytes of the rank's shards) at M <= 16, tensor (the rank's
+    share of 2MNK) at M = 4096."""
     from ashqk import tp
 
     layers = {}
@@ -584,7 +586,16 @@ def tp_mlp(world, rank, group, reps, warmup, torch, dist):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             us = float(t.item())
         flops = sum(2.0 * m * n * k for _, n, k in TP_MLP)
-        res[f"m{m}"] = {"us": round(us, 1), "tflops_total": round(flops / us / 1e6, 1)}
+        rank_bytes = (w4a16_bytes(m, TP_MLP[0][1] // world, TP_MLP[0][2], GROUP) +
+                      w4a16_bytes(m, TP_MLP[1][1], TP_MLP[1][2] // world, GROUP))
+        entry = {"us": round(us, 1), "tflops_total": round(flops / us / 1e6, 1)}
+        if m <= 16:
+            gbs = rank_bytes / us / 1e3
+            entry.update(bound="hbm", gbs_per_rank=round(gbs, 1), frac=round(gbs / hbm_peak, 3))
+        else:
+            tf = flops / world / us / 1e6
+            entry.update(bound="tensor", tflops_per_rank=round(tf, 1), frac=round(tf / tensor_peak, 3))
+        res[f"m{m}"] = entry
     del layers
     torch.cuda.empty_cache()
     return res
@@ -677,7 +688,8 @@ def run_gpu(args):
     del stack
     torch.cuda.empty_cache()
     prefill = prefill_gemm(PREFILL_M, 10, warmup, torch, tensor_peak) if world == 1 and args.only == "all" else None
-    tp_res = tp_mlp(world, rank, group, 10, warmup, torch, dist) if args.only == "all" else None
+    tp_res = (tp_mlp(world, rank, group, 10, warmup, torch, dist, hbm_peak, tensor_peak)
+              if args.only == "all" else None)
     q35 = qwen35_stack(torch, max(args.steps // 2, 10), warmup) if world == 1 and args.only == "all" else None
     marlin_res = marlin_compare(torch) if world == 1 and args.only == "all" and not args.no_marlin else None
 
@@ -735,6 +747,8 @@ def run_gpu(args):
         line["tp_mlp"] = {
             "config": "gate_up K=8192 N=57344 column-parallel + all-gather, down K=28672 N=8192 row-parallel + "
                       f"all-reduce, G=128, tp{world}, max over ranks", "per_m": tp_res,
+            "frac_of": f"per-rank roofline: {peak_kind} HBM {hbm_peak} GB/s (M <= 16), "
+                       f"{tensor_kind} tensor {tensor_peak} TFLOP/s (M = 4096); collectives included in the time",
         }
     if q35 is not None:
         line["qwen35_9b_stack"] = q35
