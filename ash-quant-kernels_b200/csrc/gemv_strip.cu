@@ -29,9 +29,10 @@
 // Programmatic dependent launch: weights, scales and zeros of the first ring
 // stages are requested before griddepcontrol.wait; x (the previous kernel's
 // output) after it; y is written only after it.
-#include <atomic>
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
+#include <mutex>
 
 #include "awq_unpack.cuh"
 #include "ll_lines.cuh"
@@ -514,7 +515,16 @@ int split_limit(int M, int stages_total) {
   return (M <= 8 && stages_total >= 32) ? 3 : 1;
 }
 
-bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p) {
+// CTAs of each kernel variant that one SM holds by registers and threads alone
+// ([M > 8][C = 4, 8, 16]; 0 = unknown: no cap). Measured on the device with
+// cudaOccupancyMaxActiveBlocksPerMultiprocessor at the first launch.
+struct StripCaps {
+  int cap[2][3];
+};
+
+int consumer_index(int c) { return c == 4 ? 0 : (c == 8 ? 1 : 2); }
+
+bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p, const StripCaps* caps = nullptr) {
   p->tiles = ceil_div(N, kStripCols);
   p->stages_total = ceil_div(K, kBoxRows);
   p->gps = (kBoxRows % G == 0) ? kBoxRows / G : kBoxRows / G + 2;
@@ -533,7 +543,7 @@ bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p) {
       break;
     }
   // CTAs that share an SM so that every CTA is resident at once.
-  const int per_sm = std::max(1, ceil_div(p->tiles * p->ksplit, sm_count));
+  int per_sm = std::max(1, ceil_div(p->tiles * p->ksplit, sm_count));
   // Consumer warps per CTA within the SM's register file (one CTA per SM and
   // M <= 8 affords 16).
   if (per_sm >= 3 || (M > 8 && per_sm >= 2))
@@ -549,6 +559,12 @@ bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p) {
                                        : (half_sm_budget() ? 110 * 1024 : 224 * 1024);
   if (max_consumers() > 0)
     while (p->consumers > 4 && p->consumers > max_consumers()) p->consumers /= 2;
+  // More CTAs than the register file holds run in waves: size the ring for the
+  // CTAs that are resident together, not for the whole grid.
+  if (caps) {
+    const int c = caps->cap[M > 8 ? 1 : 0][consumer_index(p->consumers)];
+    if (c > 0 && per_sm > c) per_sm = c;
+  }
   const size_t budget = std::min<size_t>(cap, (228 * 1024) / per_sm - 2048) - 1024;
   int ring = static_cast<int>(budget / p->stage_bytes);
   ring = std::min(ring, kMaxStages);
@@ -655,11 +671,58 @@ bool gemv_strip_eligible(const void* x, int64_t x_ld, const int32_t* qw, int64_t
 
 namespace {
 
+template <int MT, int C, bool RAW, bool PERM, bool FUSED>
+int occupancy_cap() {
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_strip_kernel<MT, C, RAW, PERM, FUSED>, 32 * (C + 1), 0) !=
+      cudaSuccess)
+    return 0;
+  return n;
+}
+
+template <bool RAW, bool PERM, bool FUSED>
+void fill_caps(StripCaps* c) {
+  c->cap[0][0] = occupancy_cap<1, 4, RAW, PERM, FUSED>();
+  c->cap[0][1] = occupancy_cap<1, 8, RAW, PERM, FUSED>();
+  c->cap[0][2] = occupancy_cap<1, 16, RAW, PERM, FUSED>();
+  c->cap[1][0] = occupancy_cap<2, 4, RAW, PERM, FUSED>();
+  c->cap[1][1] = occupancy_cap<2, 8, RAW, PERM, FUSED>();
+  c->cap[1][2] = 0;  // M > 8 never plans 16 consumer warps
+}
+
+// Register-file residency of the kernel variant this process launches, per
+// device (measured once).
+const StripCaps* strip_caps(bool fused) {
+  static StripCaps caps[64][2];
+  static std::atomic<bool> ready[64][2];
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  const int f = fused ? 1 : 0;
+  if (!ready[dev][f].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ready[dev][f].load(std::memory_order_relaxed)) {
+      StripCaps c = {};
+      if (fused)
+        fill_caps<false, false, true>(&c);
+      else if (!raw_unpack())
+        fill_caps<false, false, false>(&c);
+      else if (perm_rows())
+        fill_caps<true, true, false>(&c);
+      else
+        fill_caps<true, false, false>(&c);
+      caps[dev][f] = c;
+      ready[dev][f].store(true, std::memory_order_release);
+    }
+  }
+  return &caps[dev][f];
+}
+
 int strip_launch_impl(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
                       int64_t qz_ld, const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K, int G,
                       int sm_count, const LLPeers* ll, cudaStream_t stream) {
   StripPlan p;
-  if (!plan_strip(M, N, K, G, sm_count, &p)) return ASHQK_ERR_UNSUPPORTED;
+  if (!plan_strip(M, N, K, G, sm_count, &p, strip_caps(ll != nullptr))) return ASHQK_ERR_UNSUPPORTED;
   StripMaps maps;
   int rc = encode_tensor_map_2d(&maps.qw, CU_TENSOR_MAP_DATA_TYPE_INT32, const_cast<int32_t*>(qw), N / 8, K,
                                 static_cast<uint64_t>(qw_ld) * 4, kStripWords, kBoxRows, CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -741,14 +804,16 @@ extern "C" int ashqk_gemv_strip_plan(int M, int N, int K, int group_size, int sm
   if (!plan || M <= 0 || N <= 0 || K <= 0 || group_size <= 0 || N % 8 || K % group_size || sm_count < 0)
     return ASHQK_ERR_INVALID_ARGUMENT;
   if (M > 16 || N % 32 || group_size % 16) return ASHQK_ERR_UNSUPPORTED;
-  if (sm_count == 0) {
+  const bool on_device = sm_count == 0;
+  if (on_device) {
     ashqk::DeviceInfo info;
     const int rc = ashqk::device_info(&info);
     if (rc) return rc;
     sm_count = info.sm_count;
   }
   ashqk::StripPlan p;
-  if (!ashqk::plan_strip(M, N, K, group_size, sm_count, &p)) return ASHQK_ERR_UNSUPPORTED;
+  if (!ashqk::plan_strip(M, N, K, group_size, sm_count, &p, on_device ? ashqk::strip_caps(false) : nullptr))
+    return ASHQK_ERR_UNSUPPORTED;
   plan->grid_x = p.tiles;
   plan->grid_y = p.ksplit;
   // The launch instantiates 4 or 8 consumer warps when M > 8 (16 is planned only for M <= 8).

@@ -186,8 +186,10 @@ ASHQK_API int ashqk_dequantize_awq_f32(const int32_t* qweight, int64_t qw_ld, co
 /*
  * Launch plan of the column-strip decode GEMV (the default kernel for M <= 16
  * on 16-byte aligned operands) for an M x N x K problem with the given group
- * size on sm_count SMs (0: the current device's). Host arithmetic only: with
- * sm_count > 0 it needs no GPU. The counterpart of the reference's launch
+ * size on sm_count SMs (0: the current device's, and the plan the library
+ * launches there, which also caps CTAs per SM at what the register file holds
+ * for grids larger than that). Host arithmetic only: with sm_count > 0 it
+ * needs no GPU. The counterpart of the reference's launch
  * configuration choice, _default_config (ashqk/kernels/w4a16_gemv.py:123-129).
  * Returns ASHQK_ERR_UNSUPPORTED for problems the strip kernel does not take
  * (M > 16, N % 32, group_size % 16).
