@@ -410,25 +410,28 @@ def time_flushed(fn, reps, warmup, torch, flush):
 
 def prefill_gemm(ms, reps, warmup, torch, tensor_peak):
     """the prefill GEMM (tcgen05 kernel) on gate_up and down, TFLOP/s = 2MNK / time,
-    beside cuBLAS fp16 on the dequantised weights (x @ W_fp16)."""
+    beside cuBLAS fp16 on the dequantised weights (x @ W_fp16); SM clocks sampled over the section
+    (the GEMM is compute-bound, so its throughput follows the clock)."""
     from ashqk import _ext, w4a16_linear
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     res = {}
-    for j, (name, n, k) in enumerate(PREFILL_LAYERS):
-        qw, qz, s = random_awq(n, k, 77 + j, "cuda", torch)
-        w16 = _ext.ops().dequantize_awq(qw, qz, s, torch.float16)
-        for m in ms:
-            x = torch.randn(m, k, device="cuda").half()
-            us = time_flushed(lambda: w4a16_linear(x, qw, qz, s), reps, warmup, torch, flush)
-            us_cb = time_flushed(lambda: x @ w16, reps, warmup, torch, flush)
-            tf = 2.0 * m * n * k / us / 1e6
-            res[f"{name}_m{m}"] = {"us": round(us, 1), "tflops": round(tf, 1),
-                                   "frac_of_peak": round(tf / tensor_peak, 3),
-                                   "cublas_fp16_us": round(us_cb, 1),
-                                   "cublas_fp16_tflops": round(2.0 * m * n * k / us_cb / 1e6, 1)}
-            del x
-        del qw, qz, s, w16
+    with ClockSampler(torch.cuda.current_device()) as sampler:
+        for j, (name, n, k) in enumerate(PREFILL_LAYERS):
+            qw, qz, s = random_awq(n, k, 77 + j, "cuda", torch)
+            w16 = _ext.ops().dequantize_awq(qw, qz, s, torch.float16)
+            for m in ms:
+                x = torch.randn(m, k, device="cuda").half()
+                us = time_flushed(lambda: w4a16_linear(x, qw, qz, s), reps, warmup, torch, flush)
+                us_cb = time_flushed(lambda: x @ w16, reps, warmup, torch, flush)
+                tf = 2.0 * m * n * k / us / 1e6
+                res[f"{name}_m{m}"] = {"us": round(us, 1), "tflops": round(tf, 1),
+                                       "frac_of_peak": round(tf / tensor_peak, 3),
+                                       "cublas_fp16_us": round(us_cb, 1),
+                                       "cublas_fp16_tflops": round(2.0 * m * n * k / us_cb / 1e6, 1)}
+                del x
+            del qw, qz, s, w16
+    res["clocks"] = sampler.summary()
     del flush
     torch.cuda.empty_cache()
     return res
