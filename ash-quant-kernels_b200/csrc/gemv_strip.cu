@@ -492,6 +492,17 @@ int smem_cap_kb() {
   }();
   return v;
 }
+// Consumer warps chosen by the measured register-file residency instead of
+// the fixed rule (env ASHQK_STRIP_C_BY_REGS=1): the most warps per CTA that
+// still let every planned CTA of an SM be resident.
+bool consumers_by_regs() {
+  static const bool on = [] {
+    const char* e = std::getenv("ASHQK_STRIP_C_BY_REGS");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
 int max_consumers() {
   static const int v = [] {
     const char* e = std::getenv("ASHQK_STRIP_MAX_C");
@@ -557,6 +568,16 @@ bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p, const St
   // be resident beside it.
   const size_t cap = smem_cap_kb() > 0 ? static_cast<size_t>(smem_cap_kb()) * 1024
                                        : (half_sm_budget() ? 110 * 1024 : 224 * 1024);
+  if (caps && consumers_by_regs()) {
+    const int mt = M > 8 ? 1 : 0;
+    for (int c : {16, 8, 4}) {
+      const int cap = caps->cap[mt][consumer_index(c)];
+      if (cap >= per_sm || c == 4) {
+        p->consumers = c;
+        break;
+      }
+    }
+  }
   if (max_consumers() > 0)
     while (p->consumers > 4 && p->consumers > max_consumers()) p->consumers /= 2;
   // More CTAs than the register file holds run in waves: size the ring for the
