@@ -187,6 +187,13 @@ class P2PAllReduce:
     Every rank must construct it and call it in the same order. Tensors: fp16, contiguous, at most
     ``max_elems`` elements, a multiple of 8. The sum runs in fp32 over ranks in rank order and is
     rounded once. ``close()`` (collective) releases the regions.
+
+    Every rank must reach each call within the kernels' peer-wait limit (about 2 s of GPU time from
+    the call's launch on the waiting rank). A call whose peer does not arrive in time leaves its
+    output unwritten (in place: the local partial) and sets a sticky error bit; the kernels also
+    store that bit into a pinned host word, so the next call on this object raises RuntimeError
+    instead of summing anything, and ``check()`` raises until the error word is cleared. Under
+    CUDA-graph replay no Python code runs per call: call ``check()`` after the replays.
     """
 
     def __init__(self, group=None, max_elems: int = 1 << 16, lib=None, protocol: str = "oneshot"):
@@ -219,8 +226,10 @@ class P2PAllReduce:
         lib.ashqk_p2p_ll_region_bytes.argtypes = [ctypes.c_int64, ctypes.POINTER(ctypes.c_size_t)]
         self._region_bytes = lib.ashqk_p2p_ll_region_bytes if protocol == "ll" else lib.ashqk_p2p_region_bytes
         self._reduce = lib.ashqk_allreduce_f16_ll if protocol == "ll" else lib.ashqk_allreduce_f16_oneshot
+        lib.ashqk_set_error_mirror.argtypes = [vp]
         self._lib, self.group = lib, group
         self.rank, self.world = _world(group)
+        self._host_err, self._mirrored = None, False
         if self.world > 8:
             raise ValueError("P2PAllReduce handles at most 8 ranks (one NVLink domain of B200s)")
         self.max_elems = int(max_elems)
@@ -267,6 +276,9 @@ class P2PAllReduce:
                 raise RuntimeError("ashqk: P2P all-reduce setup failed (" + "; ".join(failed) + ")")
             dev = torch.device("cuda", torch.cuda.current_device())
             self._regions_dev = torch.tensor(ptrs, dtype=torch.int64, device=dev)
+            # Host-mapped copy of the device error word, written by a kernel only when it raises a bit.
+            self._host_err = torch.zeros(1, dtype=torch.int32).pin_memory()
+            self._mirrored = lib.ashqk_set_error_mirror(self._host_err.data_ptr()) == 0
         except BaseException:
             for p in self._imported:
                 lib.ashqk_p2p_close(p)
@@ -279,6 +291,7 @@ class P2PAllReduce:
         assert t.dtype == torch.float16 and t.is_cuda and t.is_contiguous(), "fp16 contiguous CUDA tensor"
         assert t.numel() % 8 == 0 and t.numel() <= self.max_elems, "numel: a multiple of 8, <= max_elems"
         assert self._region is not None, "P2PAllReduce is closed"
+        self._raise_if_failed()
         if out is None:
             out = torch.empty_like(t)
         assert (out.dtype == torch.float16 and out.device == t.device and out.is_contiguous()
@@ -300,6 +313,7 @@ class P2PAllReduce:
         if m > 16 or m * n > self.max_elems or x.stride(1) != 1 or any(t.stride(1) != 1 for t in
                                                                         (qweight, qzeros, scales)):
             return None
+        self._raise_if_failed()
         y = torch.empty(m, n, dtype=torch.float16, device=x.device)
         rc = self._lib.ashqk_w4a16_gemv_allreduce(
             x.data_ptr(), x.stride(0), qweight.data_ptr(), qweight.stride(0), qzeros.data_ptr(), qzeros.stride(0),
@@ -311,6 +325,11 @@ class P2PAllReduce:
         if rc != 0:
             raise RuntimeError(f"ashqk_w4a16_gemv_allreduce failed ({rc})")
         return y
+
+    def _raise_if_failed(self) -> None:
+        if self._mirrored and int(self._host_err[0]) & 4:
+            raise RuntimeError("ashqk: an earlier P2P all-reduce gave up waiting for a peer rank; its output was "
+                               "not reduced and no further calls run until the error word is cleared")
 
     def check(self) -> None:
         """Raise if a call on this device gave up waiting for a peer (the results since are invalid)."""
@@ -331,3 +350,6 @@ class P2PAllReduce:
             self._lib.ashqk_p2p_close(p)
         self._lib.ashqk_p2p_free(self._region)
         self._region, self._imported = None, []
+        if self._mirrored:
+            self._lib.ashqk_set_error_mirror(None)
+            self._mirrored = False

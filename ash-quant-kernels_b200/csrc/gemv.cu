@@ -380,9 +380,16 @@ int gemv_strip_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t 
                       int64_t qz_ld, const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K, int G,
                       int sm_count, cudaStream_t stream);
 
+bool gemv_cluster_eligible(const void* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
+                           int64_t qz_ld, const void* s, int64_t s_ld, int M, int N, int G);
+int gemv_cluster_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
+                        int64_t qz_ld, const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K,
+                        int G, int sm_count, cudaStream_t stream);
+
 namespace {
-// 0 auto (column strips, then split-K TMA, then register streaming),
-// 1 register-streaming, 2 split-K TMA, 3 column strips.
+// 0 auto (cluster-split strips, then split-K TMA, then register streaming),
+// 1 register-streaming, 2 split-K TMA, 3 column strips (whole K per CTA),
+// 4 cluster-split strips.
 int g_gemv_impl = 0;
 }
 
@@ -397,6 +404,26 @@ int gemv_workspace_bytes(int M, int N, int K, int G, int split_k, size_t* bytes)
   return ASHQK_OK;
 }
 
+bool gemv_cluster_plannable(int M, int N, int K, int G, int sm_count);
+
+// Workspace bytes the call below will use with these operands: 0 when it takes
+// the cluster-split strip kernel (which needs none), else the split-K kernels'
+// need for this problem.
+int gemv_call_workspace_bytes(const void* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
+                              int64_t qz_ld, const void* s, int64_t s_ld, int M, int N, int K, int G, int split_k,
+                              size_t* bytes) {
+  DeviceInfo info;
+  int rc = device_info(&info);
+  if (rc) return rc;
+  const bool cluster_ok = gemv_cluster_eligible(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, M, N, G);
+  if (cluster_ok && (g_gemv_impl == 4 || (g_gemv_impl == 0 && split_k <= 0)) &&
+      gemv_cluster_plannable(M, N, K, G, info.sm_count)) {
+    *bytes = 0;
+    return ASHQK_OK;
+  }
+  return gemv_workspace_bytes(M, N, K, G, split_k, bytes);
+}
+
 // M <= 16 rows, already validated.
 int gemv_launch_rows(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
                      int64_t qz_ld, const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K,
@@ -407,6 +434,13 @@ int gemv_launch_rows(const __half* x, int64_t x_ld, const int32_t* qw, int64_t q
   if (G % 16) return ASHQK_ERR_UNSUPPORTED;
   // Column strips need no workspace; a forced split_k asks for a K split, so it
   // goes to the split-K kernels.
+  const bool cluster_ok = gemv_cluster_eligible(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, M, N, G);
+  if (g_gemv_impl == 4 && !cluster_ok) return ASHQK_ERR_UNSUPPORTED;
+  if (cluster_ok && (g_gemv_impl == 4 || (g_gemv_impl == 0 && split_k <= 0))) {
+    const int rc_cl = gemv_cluster_launch(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G,
+                                          info.sm_count, stream);
+    if (!(rc_cl == ASHQK_ERR_UNSUPPORTED && g_gemv_impl == 0)) return rc_cl;
+  }
   const bool strip_ok = gemv_strip_eligible(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, M, N, G);
   if (g_gemv_impl == 3 && !strip_ok) return ASHQK_ERR_UNSUPPORTED;
   if (strip_ok && (g_gemv_impl == 3 || (g_gemv_impl == 0 && split_k <= 0))) {
@@ -471,7 +505,7 @@ int gemv_max_m() { return kMaxM; }
 extern "C" int ashqk_gemv_max_m(void) { return ashqk::kMaxM; }
 
 extern "C" int ashqk_set_gemv_kernel(int which) {
-  if (which < 0 || which > 3) return ASHQK_ERR_INVALID_ARGUMENT;
+  if (which < 0 || which > 4) return ASHQK_ERR_INVALID_ARGUMENT;
   ashqk::g_gemv_impl = which;
   return ASHQK_OK;
 }

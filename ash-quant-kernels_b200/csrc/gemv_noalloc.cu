@@ -20,7 +20,9 @@
 
 namespace ashqk {
 
-int gemv_workspace_bytes(int M, int N, int K, int G, int split_k, size_t* bytes);
+int gemv_call_workspace_bytes(const void* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
+                              int64_t qz_ld, const void* s, int64_t s_ld, int M, int N, int K, int G, int split_k,
+                              size_t* bytes);
 int gemv_launch_rows(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
                      int64_t qz_ld, const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K,
                      int G, int split_k, void* workspace, size_t ws_bytes, cudaStream_t stream);
@@ -64,13 +66,19 @@ extern "C" int ashqk_w4a16_gemv_noalloc(const void* x, int64_t x_ld, const int32
   int rc = ashqk::check_awq_args(x, x_ld, qweight, qw_ld, qzeros, qz_ld, scales, s_ld, y, y_ld, M, N, K, group_size);
   if (rc) return rc;
   const int rows = M < 16 ? M : 16;
+  // The kernel chosen for these operands decides whether any scratch is used:
+  // the cluster-split strip kernel (the default for aligned operands) needs
+  // none, so it is neither capped nor preceded by a counter clear.
   size_t need = 0;
-  rc = ashqk::gemv_workspace_bytes(rows, N, K, group_size, split_k, &need);
+  rc = ashqk::gemv_call_workspace_bytes(x, x_ld, qweight, qw_ld, qzeros, qz_ld, scales, s_ld, rows, N, K, group_size,
+                                        split_k, &need);
   if (rc) return rc;
   if (need > ashqk::kScratchBytes) return ASHQK_ERR_WORKSPACE;  // problem too large for the fixed scratch
   void* scratch = nullptr;
-  rc = ashqk::scratch_address(&scratch);
-  if (rc) return rc;
+  if (need > 0) {
+    rc = ashqk::scratch_address(&scratch);
+    if (rc) return rc;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   for (int m0 = 0; m0 < M; m0 += 16) {
     const int mc = M - m0 < 16 ? M - m0 : 16;
@@ -79,7 +87,7 @@ extern "C" int ashqk_w4a16_gemv_noalloc(const void* x, int64_t x_ld, const int32
     if (need > 0 && cudaMemsetAsync(scratch, 0, ashqk::kCounterBytes, st) != cudaSuccess) return ASHQK_ERR_CUDA;
     rc = ashqk::gemv_launch_rows(static_cast<const __half*>(x) + m0 * x_ld, x_ld, qweight, qw_ld, qzeros, qz_ld,
                                  static_cast<const __half*>(scales), s_ld, static_cast<__half*>(y) + m0 * y_ld, y_ld,
-                                 mc, N, K, group_size, split_k, scratch, ashqk::kScratchBytes, st);
+                                 mc, N, K, group_size, split_k, scratch, need > 0 ? ashqk::kScratchBytes : 0, st);
     if (rc) return rc;
   }
   return ASHQK_OK;

@@ -404,15 +404,19 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__(MT == 1 ? 112 : 168) gem
   }
 
   __syncthreads();
-  if (failed || threadIdx.x >= kTileCols) return;
+  if (threadIdx.x >= kTileCols) return;
   const int col = threadIdx.x;
   const bool col_ok = col < cols_valid;
   if (a.splits == 1) {
+    if (failed) return;
     for (int m = 0; m < a.M; ++m)
       if (col_ok) a.y[m * a.y_ld + col0 + col] = __float2half_rn(red[m * kTileCols + col]);
     return;
   }
   // ---------------- split-K through workspace slots ----------------
+  // A CTA whose pipeline gave up still takes its turn on the tile's arrival
+  // counter, so that the last arrival resets it and the workspace stays
+  // zeroed for the next call; a last arrival that itself gave up stores nothing.
   float* slot = a.ws + (static_cast<int64_t>(tile) * a.splits + split) * a.M * kTileCols;
   for (int m = 0; m < a.M; ++m) slot[m * kTileCols + col] = red[m * kTileCols + col];
   named_barrier_sync(1, kTileCols);
@@ -425,10 +429,12 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__(MT == 1 ? 112 : 168) gem
   if (!is_last) return;
   __threadfence();
   const float* tile_ws = a.ws + static_cast<int64_t>(tile) * a.splits * a.M * kTileCols;
-  for (int m = 0; m < a.M; ++m) {
-    float v = 0.f;
-    for (int s = 0; s < a.splits; ++s) v += __ldcg(tile_ws + (s * a.M + m) * kTileCols + col);
-    if (col_ok) a.y[m * a.y_ld + col0 + col] = __float2half_rn(v);
+  if (!failed) {
+    for (int m = 0; m < a.M; ++m) {
+      float v = 0.f;
+      for (int s = 0; s < a.splits; ++s) v += __ldcg(tile_ws + (s * a.M + m) * kTileCols + col);
+      if (col_ok) a.y[m * a.y_ld + col0 + col] = __float2half_rn(v);
+    }
   }
   if (threadIdx.x == 0) a.counters[tile] = 0;
 }

@@ -23,10 +23,20 @@ enum DeviceError : unsigned int {
   kDevErrPeer = 4u,          // a peer rank never arrived at an all-reduce (sticky: later calls do nothing)
 };
 extern __device__ unsigned int g_device_errors;
+// Optional host-mapped copy of the error word (ashqk_set_error_mirror): written only when a bit
+// is raised, so a host can see a failure without a copy or synchronisation in the success path.
+extern __device__ unsigned int* g_error_mirror;
 
 constexpr long long kWaitLimitCycles = 4ll * 1000 * 1000 * 1000;  // ~2 s at 1.9 GHz
 
-__device__ __forceinline__ void raise_device_error(unsigned int bits) { atomicOr(&g_device_errors, bits); }
+__device__ __forceinline__ void raise_device_error(unsigned int bits) {
+  const unsigned int old = atomicOr(&g_device_errors, bits);
+  unsigned int* mirror = *const_cast<unsigned int* volatile*>(&g_error_mirror);
+  if (mirror != nullptr) {
+    *reinterpret_cast<volatile unsigned int*>(mirror) = old | bits;
+    __threadfence_system();
+  }
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -393,6 +403,11 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16_f32(int m, int n, bool a_m
 int encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void* base, uint64_t inner_elems,
                          uint64_t outer_elems, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                          CUtensorMapSwizzle swizzle);
+
+// cuTensorMapEncodeTiled for a rank-1..5 tensor: dims[rank], strides_bytes[rank - 1] (of
+// dimensions 1..rank-1, any order of magnitudes), box[rank]; element strides 1.
+int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base, const uint64_t* dims,
+                      const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
 
 // Whether launches use programmatic dependent launch (env ASHQK_PDL=0 disables).
 bool pdl_enabled();

@@ -73,20 +73,35 @@ def cpu_model():
 
 
 # ---------------------------------------------------------------------------
-# CPU reference arm / baseline: the oracle's C restatement of ashqk/ref.py.
+# CPU reference arm / baseline: the reference's algorithm on the host cores.
 # ---------------------------------------------------------------------------
 
-def cpu_reference_sample(steps: int, warmup: int, budget_s: float | None = None):
-    """Time one decoder layer's four linear calls at M=1 on the host (all threads).
-
-    Returns (us_per_token, threads, sample_description, per_step_us list).
-    """
+def _cpu_layer_set(seed_base=0):
+    """One decoder layer's four AWQ problems at M=1 (uniform 4-bit q and z in random words,
+    scales ~ U(0.002, 0.02), x ~ N(0, 1)), as numpy arrays."""
     import numpy as np
 
+    probs = []
+    for i, (_, n, k) in enumerate(LAYERS):
+        rng = np.random.default_rng(seed_base + i)
+        x = rng.standard_normal((1, k), dtype=np.float32).astype(np.float16)
+        qw = rng.integers(0, 2 ** 32, size=(k, n // 8), dtype=np.uint32).view(np.int32)
+        qz = rng.integers(0, 2 ** 32, size=(k // GROUP, n // 8), dtype=np.uint32).view(np.int32)
+        s = rng.uniform(0.002, 0.02, size=(k // GROUP, n)).astype(np.float16)
+        probs.append((x, qw, qz, s))
+    return probs
+
+
+def cpu_reference_sample(steps: int, warmup: int, budget_s: float | None = None):
+    """Time one decoder layer's four linear calls at M=1 per step on the host (all threads), with the
+    oracle's C restatement of ashqk/ref.py (fp32 dequantisation, fp64-accumulated GEMM).
+
+    Returns (us_per_token, threads, sample_description, per_step_seconds list).
+    """
     from oracle import awq_oracle as O
 
     threads = O.c_oracle().awq_oracle_threads()
-    probs = [O.make_problem(1, n, k, GROUP, seed=i) for i, (_, n, k) in enumerate(LAYERS)]
+    probs = _cpu_layer_set()
 
     def one_layer_set():
         t0 = time.perf_counter()
@@ -102,27 +117,60 @@ def cpu_reference_sample(steps: int, warmup: int, budget_s: float | None = None)
         times.append(one_layer_set())
         if budget_s is not None and time.perf_counter() - t_start > budget_s and i >= 2:
             break
-    per_token_us = [t * N_LAYERS * 1e6 for t in times]
-    desc = (f"{len(times)} timed samples of one decoder layer's 4 linear calls (qkv, o, gate_up, down) at M=1, "
-            f"G=128, via the C oracle (fp32 dequant + fp64-accumulated GEMM, OpenMP {threads} threads), "
-            f"x36 layers; CPU: {cpu_model()}, os.cpu_count()={os.cpu_count()}")
-    del np
-    return statistics.median(per_token_us), threads, desc, per_token_us
+    desc = (f"each step: one decoder layer's 4 linear calls (qkv, o, gate_up, down) at M=1, G=128, via the C "
+            f"restatement of ashqk/ref.py (fp32 dequant + fp64 GEMM, OpenMP {threads} threads); "
+            f"us/token = 36 x median step; {len(times)} steps; CPU {cpu_model()}, "
+            f"os.cpu_count()={os.cpu_count()}")
+    return statistics.median(times) * N_LAYERS * 1e6, threads, desc, times
+
+
+def torch_ref_sample():
+    """The reference's own CPU path, ashqk/ref.py's w4a16_gemm_ref (dequantise to fp16, then x @ W)
+    and w4a16_gemm_fp32 (the fp32 truth), with torch.set_num_threads(os.cpu_count()): each of one
+    decoder layer's four calls at M=1 timed once after one untimed call; per-token figures = 36 x the
+    layer sum. The package's ashqk.ref is the same code path (no native extension is loaded)."""
+    import torch
+
+    from ashqk import ref as R
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    res = {"threads": torch.get_num_threads(), "per_layer_ms": {}}
+    tot = {"w4a16_gemm_ref": 0.0, "w4a16_gemm_fp32": 0.0}
+    for (name, _, _), (x, qw, qz, s) in zip(LAYERS, _cpu_layer_set(100)):
+        xt, qwt, qzt, st = (torch.from_numpy(a) for a in (x, qw, qz, s))
+        entry = {}
+        for fn_name in tot:
+            fn = getattr(R, fn_name)
+            fn(xt, qwt, qzt, st)
+            t0 = time.perf_counter()
+            fn(xt, qwt, qzt, st)
+            dt = time.perf_counter() - t0
+            entry[fn_name] = round(dt * 1e3, 1)
+            tot[fn_name] += dt
+        res["per_layer_ms"][name] = entry
+    res["us_per_token"] = {k: round(v * N_LAYERS * 1e6, 1) for k, v in tot.items()}
+    res["config1_qkv_m1_ms"] = res["per_layer_ms"]["qkv"]
+    return res
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    value, threads, desc, _ = cpu_reference_sample(args.steps, max(args.warmup, 1))
+    warmup = max(args.warmup, 1)
+    value, threads, desc, times = cpu_reference_sample(args.steps, warmup)
+    ms_per_step = statistics.mean(times) * 1e3
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT,
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": max(args.warmup, 1), "ms_per_step": round(value / 1e3, 3),
+        "n_gpus": args.gpus, "steps": len(times), "warmup": warmup, "ms_per_step": round(ms_per_step, 3),
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (fp16 in/out)",
         "data": "synthetic", "config": workload_config(args.gpus),  # the same workload keys as our arm
+        "step": "one decoder layer (4 linear calls) of the 36-layer token; value = 36 x median step",
         "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_torch_ref:
+        line["ref_py"] = torch_ref_sample()
     print(json.dumps(line), flush=True)
 
 
@@ -320,6 +368,57 @@ def per_layer_gemv(stack, m, torch, reps=3):
         res[name] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1), "launch": strip_plan(m, n, k)}
         del g
     return res
+
+
+DECODE_M = (1, 2, 4, 8, 16)
+
+
+def decode_sweep(stack, torch, hbm_peak, reps=5):
+    """M in {1, 2, 4, 8, 16} x {qkv, o, gate_up, down}. Per layer type and M, the
+    mean device time of one launch in a CUDA graph of 36 launches over the 36 distinct weight sets
+    (every launch streams its weights from HBM), for the W4A16 GEMV and for cuBLAS fp16 on the
+    dequantised weights (x @ W_fp16, the reference's yardstick); GB/s of the algorithmic bytes and the
+    fraction of the measured HBM peak for the sum of the four layers."""
+    from ashqk import _ext
+
+    def graph_us(calls):
+        calls[0]()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for c in calls:
+                c()
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        del g
+        return a.elapsed_time(b) * 1e3 / (reps * len(calls))
+
+    from ashqk import w4a16_linear
+
+    res = {m: {"us": [], "cublas_us": []} for m in DECODE_M}
+    for name, n, k in LAYERS:
+        w16 = [_ext.ops().dequantize_awq(*layer[name], torch.float16) for layer in stack]
+        for m in DECODE_M:
+            x = torch.randn(m, k, device="cuda").half()
+            res[m]["us"].append(round(graph_us([lambda w=layer[name]: w4a16_linear(x, *w) for layer in stack]), 2))
+            res[m]["cublas_us"].append(round(graph_us([lambda w=w: x @ w for w in w16]), 2))
+        del w16
+        torch.cuda.empty_cache()
+    out = {}
+    for m in DECODE_M:
+        nbytes = sum(w4a16_bytes(m, n, k, GROUP) for _, n, k in LAYERS)
+        gbs = nbytes / sum(res[m]["us"]) / 1e3
+        out[f"m{m}"] = {"us": res[m]["us"], "cublas_us": res[m]["cublas_us"], "gbs": round(gbs, 1),
+                        "frac": round(gbs / hbm_peak, 3),
+                        "vs_cublas": round(sum(res[m]["cublas_us"]) / sum(res[m]["us"]), 2)}
+    return out
 
 
 def strip_plan(m, n, k):
@@ -686,6 +785,7 @@ def run_gpu(args):
 
     d2h_bytes = int(out1.numel()) * out1.element_size()
     layer_bw = per_layer_gemv(stack, 1, torch) if world == 1 else None
+    sweep = decode_sweep(stack, torch, hbm_peak) if world == 1 and args.only == "all" else None
     cublas_us = cublas_fp16_stack(stack, args.steps, warmup, torch) if world == 1 else None
     n_layers = len(stack)
     del stack
@@ -714,66 +814,69 @@ def run_gpu(args):
                                      k // (world if nm in ("o", "down") else 1), GROUP)
                          for nm, n, k in LAYERS) * n_layers
     stack_gbs = per_rank_bytes / (ms1 * 1e-3) / 1e9
+    # The one JSON line (stdout) stays short enough to be read whole from the end of the log;
+    # the detail (launch shapes, per-shape breakdowns, Marlin and Qwen3.5 figures) goes to stderr.
     line = {
         "metric": METRIC, "value": round(ms1 * 1e3, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": warmup, "ms_per_step": round(ms1, 4), "higher_is_better": False, "scaling": "strong",
-        "vs_baseline": None, "dtype": "fp16 activations x int4 weights, fp32 accumulate", "data": "synthetic",
+        "vs_baseline": None, "dtype": "fp16 x int4 (AWQ), fp32 accumulate", "data": "synthetic",
         "config": workload_config(world, n_layers),
         "m4_us_per_token": round(ms4 * 1e3 / 4, 1), "m4_us_per_step": round(ms4 * 1e3, 1),
-        "stack_hbm_gbs_per_gpu": round(stack_gbs, 1),
         "stack_hbm_frac": round(stack_gbs / hbm_peak, 3),
         "gpu_launches": args.steps * len(LAYERS) * n_layers,
         "clocks": clocks.summary(),
-        "device": {"name": torch.cuda.get_device_name(device),
-                   "sm_count": torch.cuda.get_device_properties(device).multi_processor_count},
         "e2e": {"value": round(e2e_ms * 1e3, 1), "unit": UNIT, "h2d_bytes_per_step": 4096 * 2,
                 "d2h_bytes_per_step": d2h_bytes,
-                "how": f"pinned H2D of the token's hidden state + CUDA-graph replay of the "
-                       f"{len(LAYERS) * n_layers} public-API w4a16_linear calls + D2H of the last output, "
-                       "CUDA events"},
+                "how": "pinned H2D of the hidden state + graph replay of the 144 w4a16_linear calls + D2H of the output"},
     }
+    detail = {"device": {"name": torch.cuda.get_device_name(device),
+                         "sm_count": torch.cuda.get_device_properties(device).multi_processor_count},
+              "stack_hbm_gbs_per_gpu": round(stack_gbs, 1)}
     if cublas_us is not None:
         line["cublas_fp16"] = {
             "us_per_token": round(cublas_us[1], 1), "m4_us_per_step": round(cublas_us[4], 1),
-            "speedup_m1": round(cublas_us[1] / (ms1 * 1e3), 2), "speedup_m4": round(cublas_us[4] / (ms4 * 1e3), 2),
-            "how": "x @ W_fp16 (torch.matmul -> cuBLAS) on the dequantised weights of the same stack, "
-                   "same chaining, CUDA graph, CUDA events",
-        }
+            "speedup_m1": round(cublas_us[1] / (ms1 * 1e3), 2), "speedup_m4": round(cublas_us[4] / (ms4 * 1e3), 2)}
+        detail["cublas_fp16_how"] = ("x @ W_fp16 (torch.matmul -> cuBLAS) on the dequantised weights of the same "
+                                     "stack, same chaining, CUDA graph, CUDA events")
+    if sweep is not None:
+        line["decode_sweep"] = {"layers": [nm for nm, _, _ in LAYERS], **sweep}
     if prefill is not None:
-        line["prefill_gemm"] = {
-            "kernel": "gemm_tc_pair_kernel (cta_group::2, when M > 128 and the pair tiles fill half the SMs) / "
-                      "gemm_tc_kernel (one CTA per tile, K split over a cluster when tiles are few); tcgen05.mma "
-                      "with TMEM accumulators", "peak_tflops": tensor_peak,
-            "peak_kind": tensor_kind, "l2": "flushed (256 MB write) before every timed call", "shapes": prefill,
-        }
+        detail["prefill_gemm"] = prefill
+        line["prefill_gemm"] = {"m": list(PREFILL_M), "peak_tflops": tensor_peak}
+        for nm, _, _ in PREFILL_LAYERS:
+            line["prefill_gemm"][nm] = {
+                "us": [prefill[f"{nm}_m{m}"]["us"] for m in PREFILL_M],
+                "frac": [prefill[f"{nm}_m{m}"]["frac_of_peak"] for m in PREFILL_M],
+                "cublas_frac": [round(prefill[f"{nm}_m{m}"]["cublas_fp16_tflops"] / tensor_peak, 3)
+                                for m in PREFILL_M]}
     if tp_res is not None:
-        line["tp_mlp"] = {
-            "config": "gate_up K=8192 N=57344 column-parallel + all-gather, down K=28672 N=8192 row-parallel + "
-                      f"all-reduce, G=128, tp{world}, max over ranks", "per_m": tp_res,
-            "frac_of": f"per-rank roofline: {peak_kind} HBM {hbm_peak} GB/s (M <= 16), "
-                       f"{tensor_kind} tensor {tensor_peak} TFLOP/s (M = 4096); collectives included in the time",
-        }
+        detail["tp_mlp"] = tp_res
+        line["tp_mlp"] = {k: [v["us"], v["frac"]] for k, v in tp_res.items()}
     if q35 is not None:
-        line["qwen35_9b_stack"] = q35
+        detail["qwen35_9b_stack"] = q35
+        line["qwen35_9b_us"] = [q35["m1"]["us_per_step"], q35["m4"]["us_per_step"]]
     if marlin_res is not None:
-        line["marlin_vllm"] = marlin_res
+        detail["marlin_vllm"] = marlin_res
+        if "per_layer_m1_us" in marlin_res and "stack_us_per_token_est" in marlin_res:
+            line["marlin_vllm"] = {"m1_us": [marlin_res["per_layer_m1_us"].get(nm) for nm, _, _ in LAYERS],
+                                   "stack_est": marlin_res["stack_us_per_token_est"]}
     if layer_bw is not None:
         tot_bytes = sum(w4a16_bytes(1, n, k, GROUP) for _, n, k in LAYERS)
         tot_us = sum(layer_bw[nm]["us"] for nm, _, _ in LAYERS)
         achieved = tot_bytes / tot_us / 1e3
+        detail["per_layer_gemv"] = layer_bw
         line["roofline"] = {
             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 3), "peak_kind": peak_kind,
             "traffic": load_traffic(), "algorithmic_bytes": tot_bytes,
-            "per": "one launch of each layer type (qkv, o, gate_up, down) at M=1; achieved = their "
-                   "algorithmic bytes / their summed CUDA-event time",
-            "kernel": "gemv_strip_kernel (decode GEMV, M=1; all four layer types)",
-            "per_layer": layer_bw,
+            "per_layer_us": [layer_bw[nm]["us"] for nm, _, _ in LAYERS],
+            "kernel": "gemv_cluster_kernel, M=1, one launch of each layer type (qkv, o, gate_up, down)",
         }
     if layer_bw is not None and args.cpu_seconds > 0:
         value, threads, desc, _ = cpu_reference_sample(1000, 1, budget_s=args.cpu_seconds)
         line["cpu_baseline"] = {"value": round(value, 1), "unit": UNIT, "cores": threads, "kind": "port",
                                 "sample": desc}
+    print(json.dumps(detail), file=sys.stderr, flush=True)
     print(json.dumps(line), flush=True)
 
 
@@ -809,6 +912,8 @@ def main():
                     help="decode: the decode stack alone; prefill: only the prefill GEMM (profiling runs)")
     ap.add_argument("--prefill-m", type=int, nargs="*", default=None, help="M values for --only prefill")
     ap.add_argument("--no-marlin", action="store_true", help="skip the vLLM Marlin comparison")
+    ap.add_argument("--no-torch-ref", action="store_true",
+                    help="reference arm: skip the torch timing of ashqk/ref.py beside the C port")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="decoder layers in the stack (36 is the benchmark; fewer for profiling runs)")
     args = ap.parse_args()

@@ -85,15 +85,16 @@ ASHQK_API int ashqk_w4a16_gemv(const void* x, int64_t x_ld, const int32_t* qweig
  * ashqk_w4a16_gemv, but without a workspace. It is meant for callers that
  * cannot allocate device memory (a plugin that is handed only device pointers
  * by its host framework, or a caller that must not call cudaMalloc on its hot
- * path). The split-K scratch is a fixed 8 MiB array inside this library, held
- * on every GPU that loads it until the process exits; problems whose scratch
- * need exceeds it (ashqk_gemv_workspace_size() > 8 MiB) return
- * ASHQK_ERR_WORKSPACE without launching anything. The first call on a device
- * looks up that array's device address, so make it before any stream capture.
- * All calls share the array: calls that may overlap on the GPU (other
- * streams, other threads) race, so order them on one stream. Each call clears
- * the part that must start at zero. This entry point has no counterpart in the
- * reference.
+ * path). Calls that take the default cluster-split kernel (16-byte aligned
+ * operands, N % 32 == 0, group_size % 16 == 0, no split_k) use no scratch at
+ * all. The split-K kernels the other calls take use a fixed 8 MiB array inside
+ * this library, held on every GPU that loads it until the process exits;
+ * those whose scratch need exceeds it return ASHQK_ERR_WORKSPACE without
+ * launching anything. The first such call on a device looks up that array's
+ * device address, so make it before any stream capture. All calls share the
+ * array: calls that may overlap on the GPU (other streams, other threads)
+ * race, so order them on one stream. Each such call clears the part that must
+ * start at zero. This entry point has no counterpart in the reference.
  */
 ASHQK_API int ashqk_w4a16_gemv_noalloc(const void* x, int64_t x_ld, const int32_t* qweight, int64_t qw_ld,
                                        const int32_t* qzeros, int64_t qz_ld, const void* scales, int64_t s_ld,
@@ -102,11 +103,13 @@ ASHQK_API int ashqk_w4a16_gemv_noalloc(const void* x, int64_t x_ld, const int32_
 
 /*
  * Selects the decode GEMV kernel for later calls in this process: 0 = automatic
- * (column strips over the whole K when N % 32 == 0, rows are 16-byte aligned
- * and no split_k is requested; else the split-K TMA kernel when eligible; else
- * the register-streaming kernel), 1 = always register-streaming, 2 = always
- * split-K TMA, 3 = always column strips (ineligible problems then return
- * ASHQK_ERR_UNSUPPORTED). No reference counterpart: a test and tuning switch.
+ * (cluster-split column strips when N % 32 == 0, group_size % 16 == 0, rows
+ * are 16-byte aligned and no split_k is requested; else the split-K TMA kernel
+ * when eligible; else the register-streaming kernel), 1 = always
+ * register-streaming, 2 = always split-K TMA, 3 = always column strips over
+ * the whole K per CTA, 4 = always cluster-split column strips (ineligible
+ * problems then return ASHQK_ERR_UNSUPPORTED). No reference counterpart: a
+ * test and tuning switch.
  */
 ASHQK_API int ashqk_set_gemv_kernel(int which);
 
@@ -131,6 +134,16 @@ ASHQK_API int ashqk_set_gemm_kernel(int which);
  * ashqk_allreduce_f16_oneshot. No reference counterpart.
  */
 ASHQK_API int ashqk_get_device_errors(unsigned int* bits, int clear);
+
+/*
+ * Registers, for the current device, a page-locked host word (e.g. a pinned
+ * torch tensor) that receives the device error word whenever a kernel raises
+ * a bit in it -- only then, so calls that succeed pay nothing. A host can poll
+ * it before its next call instead of synchronising. NULL unregisters. Returns
+ * ASHQK_ERR_INVALID_ARGUMENT for memory the device cannot map. No reference
+ * counterpart.
+ */
+ASHQK_API int ashqk_set_error_mirror(unsigned int* host_pinned);
 
 /*
  * Bytes of workspace ashqk_w4a16_gemm may need: 0 for the tcgen05 kernel; the
@@ -205,6 +218,42 @@ typedef struct {
   int smem_bytes;      /* dynamic shared memory per CTA */
 } ashqk_strip_plan;
 ASHQK_API int ashqk_gemv_strip_plan(int M, int N, int K, int group_size, int sm_count, ashqk_strip_plan* plan);
+
+/*
+ * Launch plan of the cluster-split decode GEMV (the default kernel for M <= 16
+ * on 16-byte aligned operands with N % 32 == 0 and group_size % 16 == 0) on
+ * sm_count SMs (0: the current device's). Output tiles of 256 or 512 columns;
+ * each tile's K in stages of 32 KB of packed weights (256 or 128 rows); a
+ * cluster of cluster_ctas CTAs shares a tile, dealing its stages out in equal
+ * contiguous ranges. Host arithmetic only: with sm_count > 0 it needs no GPU.
+ * The counterpart of the reference's launch configuration choice,
+ * _default_config (ashqk/kernels/w4a16_gemv.py:123-129). Returns
+ * ASHQK_ERR_UNSUPPORTED for problems the kernel does not take.
+ */
+typedef struct {
+  int tile_cols;           /* 256 or 512 */
+  int stage_rows;          /* 256 or 128: 32 KB of packed weights per stage */
+  int tiles;               /* ceil(N / tile_cols) */
+  int stages_per_tile;     /* ceil(K / stage_rows) */
+  int cluster_ctas;        /* CTAs per thread-block cluster sharing a tile's K (1: no cluster) */
+  int ctas;                /* grid size */
+  int max_stages_per_cta;  /* the busiest CTA's stages */
+  int threads;             /* per CTA: one producer warp + 8 consumer warps */
+  int ring_stages;         /* stages resident in shared memory */
+  int stage_bytes;
+  int smem_bytes;          /* dynamic shared memory per CTA */
+} ashqk_cluster_plan;
+ASHQK_API int ashqk_gemv_cluster_plan(int M, int N, int K, int group_size, int sm_count, ashqk_cluster_plan* plan);
+
+/*
+ * Tuning of the cluster-split decode GEMV's plan for later calls in this
+ * process (0 = automatic for each): shared-memory budget per CTA in KiB
+ * (32-200), CTAs per cluster (1-16), tile columns (256 or 512), a cap on the
+ * grid's CTAs, and the stages of packed weights prefetched into L2 ahead of
+ * the shared-memory ring (-1 = automatic, 0-16). No reference counterpart: a
+ * benchmark sweep switch.
+ */
+ASHQK_API int ashqk_gemv_set_tuning(int smem_kb, int cluster_ctas, int tile_cols, int max_ctas, int prefetch_stages);
 
 /*
  * One-shot all-reduce of fp16 tensors over NVLink peer memory, for the

@@ -68,9 +68,13 @@ def test_invalid_arguments_rejected_before_launch(lib):
 
 def test_kernel_switches_validate_their_argument(lib):
     """Test and tuning switches: out-of-range choices are refused, valid ones accepted (no GPU touched)."""
-    for which in (0, 1, 2, 3):
+    for which in (0, 1, 2, 3, 4):
         assert lib.ashqk_set_gemv_kernel(which) == 0
-    assert lib.ashqk_set_gemv_kernel(4) == 1 and lib.ashqk_set_gemv_kernel(-1) == 1
+    assert lib.ashqk_set_gemv_kernel(5) == 1 and lib.ashqk_set_gemv_kernel(-1) == 1
+    assert lib.ashqk_gemv_set_tuning(0, 0, 0, 0, -1) == 0 and lib.ashqk_gemv_set_tuning(96, 3, 512, 140, 2) == 0
+    assert lib.ashqk_gemv_set_tuning(-1, 0, 0, 0, -1) == 1 and lib.ashqk_gemv_set_tuning(0, 17, 0, 0, -1) == 1
+    assert lib.ashqk_gemv_set_tuning(0, 0, 128, 0, -1) == 1 and lib.ashqk_gemv_set_tuning(0, 0, 0, 0, -2) == 1
+    assert lib.ashqk_gemv_set_tuning(0, 0, 0, 0, -1) == 0
     for which in (0, 1, 2, 3, 4):
         assert lib.ashqk_set_gemm_kernel(which) == 0
     assert lib.ashqk_set_gemm_kernel(5) == 1 and lib.ashqk_set_gemm_kernel(-1) == 1
@@ -236,3 +240,53 @@ def test_header_compiles_standalone(lang, std, tmp_path):
     r = subprocess.run([cc, std, "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-I", os.path.dirname(HEADER),
                         str(src)], capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
+
+
+class ClusterPlan(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_int) for name in ("tile_cols", "stage_rows", "tiles", "stages_per_tile", "cluster_ctas",
+                                                 "ctas", "max_stages_per_cta", "threads", "ring_stages",
+                                                 "stage_bytes", "smem_bytes")]
+
+
+def _cluster_plan(lib, m, n, k, g, sms):
+    lib.ashqk_gemv_cluster_plan.argtypes = [ctypes.c_int] * 5 + [ctypes.POINTER(ClusterPlan)]
+    p = ClusterPlan()
+    return lib.ashqk_gemv_cluster_plan(m, n, k, g, sms, ctypes.byref(p)), p
+
+
+@pytest.mark.parametrize("sms", [148, 132, 16])
+def test_cluster_plan_invariants(lib, sms):
+    """The cluster-split GEMV's plan over decode shapes and every M: 32 KB of packed weights per stage,
+    clusters of at most 16 CTAs, at most ~1.65 CTAs per SM for M <= 8 (~0.65 for M > 8) unless the
+    tiles alone exceed that, two CTAs' shared memory within an SM for M <= 8, a ring of at least two
+    stages when a CTA has two, and the busiest CTA's stages the even share of its tile."""
+    for n, k in _SHAPES:
+        for g in (32, 64, 128):
+            if k % g:
+                continue
+            for m in range(1, 17):
+                rc, p = _cluster_plan(lib, m, n, k, g, sms)
+                where = (m, n, k, g, sms)
+                assert rc == 0, where
+                assert p.tile_cols in (256, 512) and p.tile_cols * p.stage_rows // 2 == 32768, where
+                assert p.tiles == -(-n // p.tile_cols) and p.stages_per_tile == -(-k // p.stage_rows), where
+                assert 1 <= p.cluster_ctas <= min(16, p.stages_per_tile), where
+                assert p.ctas == p.tiles * p.cluster_ctas, where
+                cap = sms * 33 // 20 if m <= 8 else sms * 13 // 20
+                assert p.ctas <= cap or p.cluster_ctas == 1, where
+                assert p.max_stages_per_cta == -(-p.stages_per_tile // p.cluster_ctas), where
+                assert p.threads == 288 and 1 <= p.ring_stages <= min(8, p.max_stages_per_cta), where
+                assert p.ring_stages >= 2 or p.max_stages_per_cta == 1, where
+                assert p.stage_bytes % 1024 == 0 and p.ring_stages * p.stage_bytes + 1024 <= p.smem_bytes, where
+                if m <= 8:
+                    assert 2 * (p.smem_bytes + 516 + 1024) <= 228 * 1024, where
+                else:
+                    assert p.smem_bytes <= 201 * 1024, where
+
+
+def test_cluster_plan_rejects(lib):
+    assert _cluster_plan(lib, 17, 4096, 4096, 128, 148)[0] == 2
+    assert _cluster_plan(lib, 1, 4104, 4096, 128, 148)[0] == 2
+    assert _cluster_plan(lib, 1, 4096, 4096, 8, 148)[0] == 2
+    assert _cluster_plan(lib, 1, 4096, 4000, 128, 148)[0] == 1
+    assert _cluster_plan(lib, 0, 4096, 4096, 128, 148)[0] == 1

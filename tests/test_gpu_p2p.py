@@ -121,11 +121,17 @@ def test_missing_peer_times_out(lib):
     a = torch.ones(1024, dtype=torch.float16, device="cuda")
     out = torch.full_like(a, -7.0)
     _errors(lib, clear=True)
+    mirror = torch.zeros(1, dtype=torch.int32).pin_memory()  # host copy of the error word
+    lib.ashqk_set_error_mirror.argtypes = [ctypes.c_void_p]
+    assert lib.ashqk_set_error_mirror(mirror.data_ptr()) == 0
     t0 = time.time()
     assert _call(lib, regs, a, out) == 0                   # nothing ever sets the peer's flag
+    while int(mirror[0]) == 0 and time.time() - t0 < 30:  # seen on the host without a synchronisation
+        time.sleep(0.01)
     torch.cuda.synchronize()
     waited = time.time() - t0
     try:
+        assert int(mirror[0]) & PEER_BIT
         assert _errors(lib) & PEER_BIT
         assert 0.5 < waited < 30, waited
         assert bool((out == -7.0).all())                   # output left unwritten
@@ -138,6 +144,7 @@ def test_missing_peer_times_out(lib):
         assert regs.epoch(0) == 1 and bool((out == -7.0).all())
     finally:
         _errors(lib, clear=True)
+        assert lib.ashqk_set_error_mirror(None) == 0
     # cleared: the kernel runs again (the peer's flag now covers epoch 2)
     regs.slot(1, 0, 1024).fill_(3.0)
     assert _call(lib, regs, a, out) == 0
@@ -146,12 +153,6 @@ def test_missing_peer_times_out(lib):
 
 
 # ---- low-latency variant (ashqk_allreduce_f16_ll) -----------------------------------------------
-# Written after the last GPU session; these run when ASHQK_TEST_LL=1 until the variant has passed
-# on a GPU once.
-import os  # noqa: E402
-
-ll_pending = pytest.mark.skipif(os.environ.get("ASHQK_TEST_LL") != "1",
-                                reason="LL all-reduce awaiting its first GPU run (set ASHQK_TEST_LL=1)")
 MAX_RANKS = 8
 
 
@@ -185,7 +186,6 @@ def _call_ll(lib, regs, x, out, rank=0, world=2):
                                       regs.max_elems, torch.cuda.current_stream().cuda_stream)
 
 
-@ll_pending
 def test_ll_protocol_and_sum(lib):
     assert _errors(lib, clear=True) & PEER_BIT == 0
     regs = _LLRegions(lib, 1 << 15)
@@ -210,7 +210,6 @@ def test_ll_protocol_and_sum(lib):
     assert torch.equal(a, ref) and _errors(lib) & PEER_BIT == 0
 
 
-@ll_pending
 def test_ll_missing_peer_times_out(lib):
     regs = _LLRegions(lib, 1024)
     a = torch.ones(1024, dtype=torch.float16, device="cuda")
@@ -243,11 +242,10 @@ def _fused_call(lib, regs, x, qw, qz, s, y, rank=0, world=2):
                                           torch.cuda.current_stream().cuda_stream)
 
 
-@ll_pending
 @pytest.mark.parametrize("m,n,k", [(1, 4096, 2048), (4, 4096, 6144), (16, 4096, 512), (2, 96, 1024)])
 def test_fused_row_parallel_gemv(lib, m, n, k):
-    """Rank 0 of two with the host playing rank 1: the fused kernel's y equals the unfused GEMV's
-    fp16 partial plus rank 1's, summed in fp32 and rounded once; the lines it pushed carry its
+    """Rank 0 of two with the host playing rank 1: the fused kernel's y equals the unfused
+    column-strip GEMV's fp16 partial plus rank 1's, summed in fp32 and rounded once; the lines it pushed carry its
     partial; the region's call counter advances once per call (shared with the LL all-reduce)."""
     import ashqk
     from tests._helpers import quantized_problem, to_cuda
@@ -256,8 +254,13 @@ def test_fused_row_parallel_gemv(lib, m, n, k):
     regs = _LLRegions(lib, 1 << 16)
     x0, qw0, qz0, s0 = to_cuda(*quantized_problem(m, n, k, 128, seed=m + 1))
     x1, qw1, qz1, s1 = to_cuda(*quantized_problem(m, n, k, 128, seed=m + 101))
-    y0 = ashqk.w4a16_linear(x0, qw0, qz0, s0)   # this rank's partial, as the unfused GEMV stores it
-    y1 = ashqk.w4a16_linear(x1, qw1, qz1, s1)   # the peer's
+    # The fused epilogue is the column-strip GEMV's (kernel 3): its partial is bitwise that kernel's.
+    assert lib.ashqk_set_gemv_kernel(3) == 0
+    try:
+        y0 = ashqk.w4a16_linear(x0, qw0, qz0, s0)   # this rank's partial, as the unfused GEMV stores it
+        y1 = ashqk.w4a16_linear(x1, qw1, qz1, s1)   # the peer's
+    finally:
+        assert lib.ashqk_set_gemv_kernel(0) == 0
     for e in (1, 2, 3):
         regs.lines(0, e & 1, 1)[: m * n // 2] = _pack_lines(y1, e)
         y = torch.full((m, n), float("nan"), dtype=torch.float16, device="cuda")
@@ -269,7 +272,6 @@ def test_fused_row_parallel_gemv(lib, m, n, k):
     assert _errors(lib) == 0
 
 
-@ll_pending
 def test_fused_declines_what_it_cannot_take(lib):
     regs = _LLRegions(lib, 1 << 12)
     x = torch.zeros(2, 1024, dtype=torch.float16, device="cuda")

@@ -169,7 +169,7 @@ def _c_lib():
     return ctypes.CDLL(_ext.C_LIBRARY)
 
 
-@pytest.fixture(params=[1, 2, 3], ids=["regstream", "tma", "strip"])
+@pytest.fixture(params=[1, 2, 3, 4], ids=["regstream", "tma", "strip", "cluster"])
 def gemv_kernel(request):
     """Run a test once per decode-GEMV kernel (ashqk_set_gemv_kernel), then restore auto."""
     lib = _c_lib()

@@ -206,10 +206,17 @@ def _p2p_worker(rank, world, port, protocol="oneshot"):
         y_p2p = tp.row_parallel_linear(xs, *sh, allreduce=ar)
         y_nccl = tp.row_parallel_linear(xs, *sh, reduce_dtype=torch.float32)
         assert float((y_p2p.float() - y_nccl.float()).abs().max()) <= 1e-2 * float(y_nccl.float().abs().max())
-        if protocol == "ll":  # the fused GEMV + all-reduce equals the two steps bit for bit
-            from ashqk import w4a16_linear
+        if protocol == "ll":  # the fused GEMV + all-reduce equals the column-strip GEMV + all-reduce bit for bit
+            import ctypes
 
-            assert torch.equal(y_p2p, ar(w4a16_linear(xs, *sh)))
+            from ashqk import _ext, w4a16_linear
+
+            lib = ctypes.CDLL(_ext.C_LIBRARY)
+            assert lib.ashqk_set_gemv_kernel(3) == 0
+            try:
+                assert torch.equal(y_p2p, ar(w4a16_linear(xs, *sh)))
+            finally:
+                assert lib.ashqk_set_gemv_kernel(0) == 0
         ar.check()
         ar.close()
         dist.barrier()
@@ -220,8 +227,7 @@ def _p2p_worker(rank, world, port, protocol="oneshot"):
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2+ GPUs")
 @pytest.mark.parametrize("protocol", [
     "oneshot",
-    pytest.param("ll", marks=pytest.mark.skipif(os.environ.get("ASHQK_TEST_LL") != "1",
-                                                reason="LL all-reduce awaiting its first GPU run")),
+    "ll",
 ])
 def test_p2p_allreduce(protocol):
     import torch.multiprocessing as mp

@@ -84,6 +84,7 @@ class _FakeP2PLib:
         self.ashqk_w4a16_gemv_allreduce = lambda *args: 0
         self.ashqk_p2p_ll_region_bytes = region_bytes
         self.ashqk_get_device_errors = nop
+        self.ashqk_set_error_mirror = nop
 
 
 def _worker(rank, port, case):
