@@ -89,6 +89,16 @@ __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
   return v;
 }
 
+// D = A(16x16, row) * B(16x8, col), fp16 inputs, fp32 result (no accumulator input).
+__device__ __forceinline__ void mma_16816_first(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  const float z = 0.f;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%10, %10, %10, %10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z));
+}
+
 // D = A(16x16, row) * B(16x8, col) + C, fp16 inputs, fp32 accumulate.
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(

@@ -327,19 +327,24 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
       for (int j = 0; j < 4; ++j) {
         // column 2 j + hA of the word: half hA of scale component j, nibble 4 hA + j of the zero word
         const float f = (j & 1) ? 0.0625f : 1.f;
-        const float c = (j & 1) ? 64.f : 1024.f;
         const float s_a = half_bits_to_float(sav[j] >> (16 * hA));
         const float s_b = half_bits_to_float(sbv[j] >> (16 * hA));
+        // c + z exactly: z ORed into the mantissa of 1024.0f (unit 2^-13 there) or of 64.0f (2^-17)
+        const uint32_t base_bits = (j & 1) ? 0x42800000u : 0x44800000u;
+        const int sh = (j & 1) ? 17 : 13;
+        const float cz_a = __uint_as_float(base_bits | (((za >> (4 * j)) & 15u) << sh));
+        const float cz_b = __uint_as_float(base_bits | (((zb >> (4 * j)) & 15u) << sh));
         ca[j] = s_a * f;
-        cb[j] = -s_a * (c + static_cast<float>((za >> (4 * j)) & 15u));
+        cb[j] = -s_a * cz_a;
         ca[4 + j] = s_b * f;
-        cb[4 + j] = -s_b * (c + static_cast<float>((zb >> (4 * j)) & 15u));
+        cb[4 + j] = -s_b * cz_b;
       }
     };
 
     const uint32_t ones_a[4] = {kOneX2, kOneX2, kOneX2, kOneX2};
-    // One 16-row step: the weights R4 of this lane against the x fragments b0, b1.
-    auto step = [&](const uint32_t (&R4)[4], const uint32_t (&bx)[MT][4], int h) {
+    // One 16-row step: the weights R4 of this lane against the x fragments b0, b1; `first`
+    // starts the block's sums from zero instead of adding to them.
+    auto step = [&](const uint32_t (&R4)[4], const uint32_t (&bx)[MT][4], int h, bool first) {
       uint32_t R8[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) R8[i] = R4[i] >> 8;
@@ -350,10 +355,36 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
 #pragma unroll
         for (int i = 0; i < 4; ++i) A[i] = lop3_and_or(j < 2 ? R4[i] : R8[i], mask, kMagic1024x2);
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) mma_16816(part[mt][j], A, bx[mt][2 * h], bx[mt][2 * h + 1]);
+        for (int mt = 0; mt < MT; ++mt) {
+          if (first)
+            mma_16816_first(part[mt][j], A, bx[mt][2 * h], bx[mt][2 * h + 1]);
+          else
+            mma_16816(part[mt][j], A, bx[mt][2 * h], bx[mt][2 * h + 1]);
+        }
       }
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) mma_16816(psx[mt], ones_a, bx[mt][2 * h], bx[mt][2 * h + 1]);
+      for (int mt = 0; mt < MT; ++mt) {
+        if (first)
+          mma_16816_first(psx[mt], ones_a, bx[mt][2 * h], bx[mt][2 * h + 1]);
+        else
+          mma_16816(psx[mt], ones_a, bx[mt][2 * h], bx[mt][2 * h + 1]);
+      }
+    };
+    // Whole-block groups (G % 128 == 0): fold the block's sums into acc with its group's scale and
+    // zero point, read from the stage now (nothing to zero: the next block starts from zero).
+    auto fold_block = [&](uint32_t base, int gslot) {
+      load_group(base, gslot);
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[mt][j][0] = fmaf(ca[j], part[mt][j][0], fmaf(cb[j], psx[mt][0], acc[mt][j][0]));
+          acc[mt][j][2] = fmaf(ca[4 + j], part[mt][j][2], fmaf(cb[4 + j], psx[mt][0], acc[mt][j][2]));
+          if (TOKS > 1) {
+            acc[mt][j][1] = fmaf(ca[j], part[mt][j][1], fmaf(cb[j], psx[mt][1], acc[mt][j][1]));
+            acc[mt][j][3] = fmaf(ca[4 + j], part[mt][j][3], fmaf(cb[4 + j], psx[mt][1], acc[mt][j][3]));
+          }
+        }
     };
 
     int cur_grp = -1;
@@ -375,7 +406,6 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
       const int gbase = k0 / G;
       const uint32_t wbase = base + w_lane;
       const uint32_t xbase = base + x_off;
-      if (GB) enter_group(base, kb, gbase);
       // Loads run one step pair ahead of the arithmetic.
       uint32_t bx[MT][4], Ra[4], Rb[4];
 #pragma unroll
@@ -392,9 +422,9 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
           ldsm_x4_trans(wbase + (s + 3) * kStepBytes, Rbn);
         }
         if (!GB) enter_group(base, kb + 16 * s, gbase);
-        step(Ra, bx, 0);
+        step(Ra, bx, 0, GB && s == 0);
         if (!GB) enter_group(base, kb + 16 * (s + 1), gbase);
-        step(Rb, bx, 1);
+        step(Rb, bx, 1, false);
         if (s + 2 < kBlockRows / 16) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -405,10 +435,11 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
           }
         }
       }
+      if (GB) fold_block(base, kb / G - gbase);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
-    if (cur_grp >= 0) flush();
+    if (!GB && cur_grp >= 0) flush();
   }
 
   // ---------------- the cluster's sum ----------------
