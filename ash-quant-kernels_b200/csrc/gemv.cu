@@ -516,23 +516,12 @@ extern "C" int ashqk_gemv_workspace_size(int M, int N, int K, int group_size, in
   return ashqk::gemv_workspace_bytes(M, N, K, group_size, split_k, bytes);
 }
 
-namespace ashqk {
-bool l2_prefetch_enabled();
-int l2_prefetch_launch(const int32_t* qw, int64_t qw_ld, const int32_t* qz, int64_t qz_ld, const __half* s,
-                       int64_t s_ld, int N, int K, int G, cudaStream_t stream);
-}  // namespace ashqk
-
 extern "C" int ashqk_w4a16_gemv(const void* x, int64_t x_ld, const int32_t* qweight, int64_t qw_ld,
                                 const int32_t* qzeros, int64_t qz_ld, const void* scales, int64_t s_ld, void* y,
                                 int64_t y_ld, int M, int N, int K, int group_size, int split_k, void* workspace,
                                 size_t workspace_bytes, void* stream) {
   int rc = ashqk::check_awq_args(x, x_ld, qweight, qw_ld, qzeros, qz_ld, scales, s_ld, y, y_ld, M, N, K, group_size);
   if (rc) return rc;
-  if (ashqk::l2_prefetch_enabled()) {
-    rc = ashqk::l2_prefetch_launch(qweight, qw_ld, qzeros, qz_ld, static_cast<const __half*>(scales), s_ld, N, K,
-                                   group_size, static_cast<cudaStream_t>(stream));
-    if (rc) return rc;
-  }
   // Rows beyond 16 are processed 16 at a time (each chunk re-reads the weights).
   for (int m0 = 0; m0 < M; m0 += ashqk::kMaxM) {
     const int mc = std::min(ashqk::kMaxM, M - m0);

@@ -104,26 +104,10 @@ __device__ void strip_allreduce_store(const Args& a, const float* tile_sum, int 
   }
 }
 
-// RAW: feed the magic-number halves (1024 + q, 1024 + 16 q) to the mma without
-// subtracting the zero point per weight, accumulate each group's sum of x with
-// one more mma against a fragment of ones, and correct once per group:
-// sum x (q - z) = f * dot - (c + z) * sum x, with f = 1, c = 1024 for the
-// low-nibble columns (0, 1, 4, 5 of a word) and f = 1/16, c = 64 for the
-// high-nibble ones (2, 3, 6, 7). 16 fewer instructions per 16-row step.
-//
-// PERM: permute k inside every 16-row step so that the four rows a lane reads
-// are t, t+4, t+8, t+12 (banks 8t..8t+7: conflict-free) instead of 2t, 2t+1,
-// 2t+8, 2t+9 (lanes t and t+2 share banks). Any k order gives the same dot
-// product as long as x follows it, so the warp owning a slot rewrites that
-// stage's x once before its steps: each 16-value block becomes
-// (x0, x4, x1, x5, x2, x6, x3, x7, x8, x12, ...), and token m's 16-byte chunk
-// c moves to chunk c ^ (m & 7) so that the 8 tokens of an mma fragment, 512
-// bytes apart, also read distinct banks.
-//
 // FUSED: row-parallel tensor parallelism -- y is this rank's partial over its K
 // shard, summed over the ranks in the epilogue (strip_allreduce_store) before
 // it is stored.
-template <int MT, int C, bool RAW, bool PERM, bool FUSED>
+template <int MT, int C, bool FUSED>
 __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_constant__ StripMaps maps,
                                                                   const StripArgs a) {
   extern __shared__ unsigned char smem_raw[];
@@ -209,7 +193,7 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
     uint32_t roff[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q)
-      roff[q] = (PERM ? t + 4 * q : 2 * t + (q & 1) + 8 * (q >> 1)) * (kStripWords * 4) + 4 * g;
+      roff[q] = (2 * t + (q & 1) + 8 * (q >> 1)) * (kStripWords * 4) + 4 * g;
     bool xok[MT];
     uint32_t xrow[MT];
 #pragma unroll
@@ -224,13 +208,7 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
       for (int j = 0; j < 4; ++j)
 #pragma unroll
         for (int r = 0; r < 4; ++r) part[mt][j][r] = 0.f;
-    float psx[MT][4];  // RAW: the group's sum of x per token (c0: token 8mt+2t, c1: 8mt+2t+1)
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) psx[mt][r] = 0.f;
-    uint32_t zc[8];   // zero-point constants (subtracting variant)
-    float zk[8];      // RAW: c + z of columns 0..7 of word g
+    uint32_t zc[8];  // zero-point constants
     uint32_t sh[4];
     int cur_grp = -1;
 
@@ -246,14 +224,6 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
       for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          if (RAW) {
-            // mma j holds column j (rows g) and j + 4 (rows g + 8) of word g.
-            const float f = j < 2 ? 1.f : 0.0625f;
-            part[mt][j][0] = fmaf(part[mt][j][0], f, -zk[j] * psx[mt][0]);
-            part[mt][j][1] = fmaf(part[mt][j][1], f, -zk[j] * psx[mt][1]);
-            part[mt][j][2] = fmaf(part[mt][j][2], f, -zk[4 + j] * psx[mt][0]);
-            part[mt][j][3] = fmaf(part[mt][j][3], f, -zk[4 + j] * psx[mt][1]);
-          }
           acc[mt][j][0] = fmaf(sc[j], part[mt][j][0], acc[mt][j][0]);
           acc[mt][j][1] = fmaf(sc[j], part[mt][j][1], acc[mt][j][1]);
           acc[mt][j][2] = fmaf(sc[4 + j], part[mt][j][2], acc[mt][j][2]);
@@ -261,9 +231,6 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
 #pragma unroll
           for (int r = 0; r < 4; ++r) part[mt][j][r] = 0.f;
         }
-        if (RAW)
-#pragma unroll
-          for (int r = 0; r < 4; ++r) psx[mt][r] = 0.f;
       }
     };
 
@@ -275,23 +242,6 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
       const int slot = li - round;  // round = the first stage of this pass over the ring
       if (!mbar_wait(&full[slot], (li / a.ring) & 1, &abort_flag)) break;
       const uint32_t base = smem_s + slot * a.stage_bytes;
-      if (PERM) {
-        // Rewrite this stage's x in the permuted, chunk-rotated order (row m:
-        // 32 chunks of 8 halves; lane l takes chunk l).
-        const uint32_t xb = base + a.x_off;
-        for (int m = 0; m < a.M; ++m) {
-          const uint4 v = lds_v4(xb + m * kXRowBytes + lane * 16);
-          uint4 o;
-          o.x = prmt(v.x, v.z, 0x5410u);  // (x0, x4)
-          o.y = prmt(v.x, v.z, 0x7632u);  // (x1, x5)
-          o.z = prmt(v.y, v.w, 0x5410u);  // (x2, x6)
-          o.w = prmt(v.y, v.w, 0x7632u);  // (x3, x7)
-          __syncwarp();  // every lane has read row m before any lane writes it
-          sts_v4(xb + m * kXRowBytes + ((lane ^ (m & 7)) * 16), o);
-        }
-        fence_proxy_async_smem();  // the slot's next TMA fill comes after these writes
-        __syncwarp();
-      }
       const int k0 = (sb + li) * kBoxRows;
       const int gbase = k0 / a.G;
       const int steps = min(kBoxRows, a.K - k0) / 16;  // K is a multiple of 16
@@ -304,14 +254,7 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
           grp_end = (grp + 1) * a.G;
           const uint32_t gslot = static_cast<uint32_t>(grp - gbase);
           const uint32_t zw = lds_u32(base + a.z_off + gslot * (kStripWords * 4) + 4 * g);
-          if (RAW) {
-            // Column c of the word sits in nibble kAwqNibbleOfCol[c] (AWQ order).
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-              zk[c] = static_cast<float>((zw >> (4 * kAwqNibbleOfCol[c])) & 15u) + ((c & 2) ? 64.f : 1024.f);
-          } else {
-            zero_consts(zw, zc);
-          }
+          zero_consts(zw, zc);
           const uint4 sv = lds_v4(base + a.s_off + gslot * (kStripCols * 2) + 16 * g);
           sh[0] = sv.x;
           sh[1] = sv.y;
@@ -324,42 +267,25 @@ __global__ void __launch_bounds__(32 * (C + 1)) gemv_strip_kernel(const __grid_c
 #pragma unroll
         for (int q = 0; q < 4; ++q) w[q] = lds_u32(wrow + roff[q]);
         uint32_t oa[4], ob[4], oc[4], od[4];
-        if (RAW) {
-          unpack_raw(prmt(w[0], w[1], 0x6420u), oa);
-          unpack_raw(prmt(w[0], w[1], 0x7531u), ob);
-          unpack_raw(prmt(w[2], w[3], 0x6420u), oc);
-          unpack_raw(prmt(w[2], w[3], 0x7531u), od);
-        } else {
-          const uint32_t za[4] = {zc[0], zc[1], zc[2], zc[3]};
-          const uint32_t zb[4] = {zc[4], zc[5], zc[6], zc[7]};
-          unpack_pairs(prmt(w[0], w[1], 0x6420u), za, oa);
-          unpack_pairs(prmt(w[0], w[1], 0x7531u), zb, ob);
-          unpack_pairs(prmt(w[2], w[3], 0x6420u), za, oc);
-          unpack_pairs(prmt(w[2], w[3], 0x7531u), zb, od);
-        }
+        const uint32_t za[4] = {zc[0], zc[1], zc[2], zc[3]};
+        const uint32_t zb[4] = {zc[4], zc[5], zc[6], zc[7]};
+        unpack_pairs(prmt(w[0], w[1], 0x6420u), za, oa);
+        unpack_pairs(prmt(w[0], w[1], 0x7531u), zb, ob);
+        unpack_pairs(prmt(w[2], w[3], 0x6420u), za, oc);
+        unpack_pairs(prmt(w[2], w[3], 0x7531u), zb, od);
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
           uint32_t b0 = 0u, b1 = 0u;
           if (xok[mt]) {
-            if (PERM) {  // chunks 2s and 2s+1 of token 8mt+g, rotated by g
-              const uint32_t xa = base + a.x_off + xrow[mt];
-              b0 = lds_u32(xa + ((static_cast<uint32_t>(2 * s) ^ g) << 4));
-              b1 = lds_u32(xa + ((static_cast<uint32_t>(2 * s + 1) ^ g) << 4));
-            } else {
-              const uint32_t xa = base + a.x_off + xrow[mt] + s * 32;
-              b0 = lds_u32(xa);
-              b1 = lds_u32(xa + 16);
-            }
+            const uint32_t xa = base + a.x_off + xrow[mt] + s * 32;
+            b0 = lds_u32(xa);
+            b1 = lds_u32(xa + 16);
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int sl = ((j & 1) << 1) | (j >> 1);
             const uint32_t A[4] = {oa[sl], ob[sl], oc[sl], od[sl]};
             mma_16816(part[mt][j], A, b0, b1);
-          }
-          if (RAW) {
-            const uint32_t ones[4] = {kOneX2, kOneX2, kOneX2, kOneX2};
-            mma_16816(psx[mt], ones, b0, b1);
           }
         }
       }
@@ -467,64 +393,11 @@ struct StripPlan {
 
 int align128(int v) { return (v + 127) / 128 * 128; }
 
-bool wide_consumers() {
-  static const bool on = [] {
-    const char* e = std::getenv("ASHQK_STRIP_C16");
-    return !(e && e[0] == '0');
-  }();
-  return on;
-}
-
-bool half_sm_budget() {
-  static const bool on = [] {
-    const char* e = std::getenv("ASHQK_STRIP_HALF");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
-
-// Tuning knobs for the co-residency experiments (env; 0 = unset).
-int smem_cap_kb() {
-  static const int v = [] {
-    const char* e = std::getenv("ASHQK_STRIP_SMEM_CAP_KB");
-    const int x = e ? std::atoi(e) : 0;
-    return x >= 32 && x <= 224 ? x : 0;
-  }();
-  return v;
-}
-// Consumer warps chosen by the measured register-file residency instead of
-// the fixed rule (env ASHQK_STRIP_C_BY_REGS=1): the most warps per CTA that
-// still let every planned CTA of an SM be resident.
-bool consumers_by_regs() {
-  static const bool on = [] {
-    const char* e = std::getenv("ASHQK_STRIP_C_BY_REGS");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
-
-int max_consumers() {
-  static const int v = [] {
-    const char* e = std::getenv("ASHQK_STRIP_MAX_C");
-    const int x = e ? std::atoi(e) : 0;
-    return x == 4 || x == 8 || x == 16 ? x : 0;
-  }();
-  return v;
-}
-
 // CTAs per SM a K split may reach: 3 for deep layers at M <= 8 (>= 32 stages,
 // K >= 8192: measured 14.1 -> 13.6 us on 4096 x 12288 at M=1), else 1
 // (shallower layers, and M > 8 with its twice larger stages, lose more to
-// sharing SMs than they gain). Env ASHQK_STRIP_SPLIT_LIMIT overrides.
-int split_limit(int M, int stages_total) {
-  static const int v = [] {
-    const char* e = std::getenv("ASHQK_STRIP_SPLIT_LIMIT");
-    const int x = e ? std::atoi(e) : 0;
-    return x >= 1 && x <= 4 ? x : 0;
-  }();
-  if (v) return v;
-  return (M <= 8 && stages_total >= 32) ? 3 : 1;
-}
+// sharing SMs than they gain).
+int split_limit(int M, int stages_total) { return (M <= 8 && stages_total >= 32) ? 3 : 1; }
 
 // CTAs of each kernel variant that one SM holds by registers and threads alone
 // ([M > 8][C = 4, 8, 16]; 0 = unknown: no cap). Measured on the device with
@@ -559,27 +432,11 @@ bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p, const St
   // M <= 8 affords 16).
   if (per_sm >= 3 || (M > 8 && per_sm >= 2))
     p->consumers = 4;
-  else if (per_sm == 1 && M <= 8 && wide_consumers())
+  else if (per_sm == 1 && M <= 8)
     p->consumers = 16;
   else
     p->consumers = 8;
-  // With half_sm (or an explicit cap), a CTA takes at most that much shared
-  // memory so that the next kernel's CTAs (programmatic dependent launch) can
-  // be resident beside it.
-  const size_t cap = smem_cap_kb() > 0 ? static_cast<size_t>(smem_cap_kb()) * 1024
-                                       : (half_sm_budget() ? 110 * 1024 : 224 * 1024);
-  if (caps && consumers_by_regs()) {
-    const int mt = M > 8 ? 1 : 0;
-    for (int c : {16, 8, 4}) {
-      const int cap = caps->cap[mt][consumer_index(c)];
-      if (cap >= per_sm || c == 4) {
-        p->consumers = c;
-        break;
-      }
-    }
-  }
-  if (max_consumers() > 0)
-    while (p->consumers > 4 && p->consumers > max_consumers()) p->consumers /= 2;
+  const size_t cap = 224 * 1024;
   // More CTAs than the register file holds run in waves: size the ring for the
   // CTAs that are resident together, not for the whole grid.
   if (caps) {
@@ -601,13 +458,13 @@ bool plan_strip(int M, int N, int K, int G, int sm_count, StripPlan* p, const St
   return true;
 }
 
-template <int MT, int C, bool RAW, bool PERM, bool FUSED>
+template <int MT, int C, bool FUSED>
 int launch_strip_t(const StripMaps& maps, const StripArgs& args, int tiles, size_t smem, cudaStream_t stream) {
   const int ks = args.ksplit;
   static std::atomic<bool> configured[64];  // zero-initialised (static storage)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ASHQK_ERR_CUDA;
-  auto kernel = gemv_strip_kernel<MT, C, RAW, PERM, FUSED>;
+  auto kernel = gemv_strip_kernel<MT, C, FUSED>;
   if (!configured[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
@@ -657,29 +514,10 @@ int launch_strip_t(const StripMaps& maps, const StripArgs& args, int tiles, size
   return ASHQK_OK;
 }
 
-bool raw_unpack() {
-  static const bool on = [] {
-    const char* e = std::getenv("ASHQK_STRIP_RAW");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
-
-// Permuted k order (env ASHQK_STRIP_PERM=1, together with ASHQK_STRIP_RAW=1).
-bool perm_rows() {
-  static const bool on = [] {
-    const char* e = std::getenv("ASHQK_STRIP_PERM");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
-
 template <int MT, int C>
 int launch_strip(const StripMaps& maps, const StripArgs& args, int tiles, size_t smem, cudaStream_t stream) {
-  if (args.ll.regions != nullptr) return launch_strip_t<MT, C, false, false, true>(maps, args, tiles, smem, stream);
-  if (!raw_unpack()) return launch_strip_t<MT, C, false, false, false>(maps, args, tiles, smem, stream);
-  return perm_rows() ? launch_strip_t<MT, C, true, true, false>(maps, args, tiles, smem, stream)
-                     : launch_strip_t<MT, C, true, false, false>(maps, args, tiles, smem, stream);
+  if (args.ll.regions != nullptr) return launch_strip_t<MT, C, true>(maps, args, tiles, smem, stream);
+  return launch_strip_t<MT, C, false>(maps, args, tiles, smem, stream);
 }
 
 }  // namespace
@@ -692,22 +530,22 @@ bool gemv_strip_eligible(const void* x, int64_t x_ld, const int32_t* qw, int64_t
 
 namespace {
 
-template <int MT, int C, bool RAW, bool PERM, bool FUSED>
+template <int MT, int C, bool FUSED>
 int occupancy_cap() {
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_strip_kernel<MT, C, RAW, PERM, FUSED>, 32 * (C + 1), 0) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_strip_kernel<MT, C, FUSED>, 32 * (C + 1), 0) !=
       cudaSuccess)
     return 0;
   return n;
 }
 
-template <bool RAW, bool PERM, bool FUSED>
+template <bool FUSED>
 void fill_caps(StripCaps* c) {
-  c->cap[0][0] = occupancy_cap<1, 4, RAW, PERM, FUSED>();
-  c->cap[0][1] = occupancy_cap<1, 8, RAW, PERM, FUSED>();
-  c->cap[0][2] = occupancy_cap<1, 16, RAW, PERM, FUSED>();
-  c->cap[1][0] = occupancy_cap<2, 4, RAW, PERM, FUSED>();
-  c->cap[1][1] = occupancy_cap<2, 8, RAW, PERM, FUSED>();
+  c->cap[0][0] = occupancy_cap<1, 4, FUSED>();
+  c->cap[0][1] = occupancy_cap<1, 8, FUSED>();
+  c->cap[0][2] = occupancy_cap<1, 16, FUSED>();
+  c->cap[1][0] = occupancy_cap<2, 4, FUSED>();
+  c->cap[1][1] = occupancy_cap<2, 8, FUSED>();
   c->cap[1][2] = 0;  // M > 8 never plans 16 consumer warps
 }
 
@@ -725,13 +563,9 @@ const StripCaps* strip_caps(bool fused) {
     if (!ready[dev][f].load(std::memory_order_relaxed)) {
       StripCaps c = {};
       if (fused)
-        fill_caps<false, false, true>(&c);
-      else if (!raw_unpack())
-        fill_caps<false, false, false>(&c);
-      else if (perm_rows())
-        fill_caps<true, true, false>(&c);
+        fill_caps<true>(&c);
       else
-        fill_caps<true, false, false>(&c);
+        fill_caps<false>(&c);
       caps[dev][f] = c;
       ready[dev][f].store(true, std::memory_order_release);
     }

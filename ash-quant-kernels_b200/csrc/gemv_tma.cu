@@ -18,12 +18,10 @@
 //    mma.sync A fragment, so x needs no permutation. Unpacking (prmt + LOP3
 //    magic exponent + HSUB2/HFMA2) and mma.sync m16n8k16 are shared with
 //    csrc/gemv.cu (csrc/awq_unpack.cuh).
-//  * split-K: the CTAs of one column tile form a thread-block cluster along K
-//    (up to 16). Each CTA leaves its partial tile in its shared memory; after a
-//    cluster barrier, CTA r sums column slice r over all CTAs through DSMEM in
-//    fixed rank order (deterministic) and stores y. No workspace, no atomics.
-//    More than 16 splits fall back to fp32 workspace slots finished by the
-//    last-arriving CTA.
+//  * split-K (the caller's split_k, or about one CTA per SM): each CTA writes
+//    its partial tile to an fp32 workspace slot; the last CTA to arrive on the
+//    tile's counter sums the slots in split order (deterministic), stores y and
+//    resets the counter.
 //  * programmatic dependent launch: dependents may launch at once; only x (the
 //    previous kernel's output), y and the workspace are touched after
 //    griddepcontrol.wait, so the next layer's weights stream during this
@@ -59,7 +57,6 @@ constexpr int kStageBytes = kBoxBytes * kBoxes;
 constexpr int kStages = ASHQK_GEMV_STAGES;
 static_assert(kBoxes == 1 || kBoxes % 2 == 0, "stages hold one box or an even number of boxes");
 constexpr int kMaxTiles = 16384;
-constexpr int kMaxCluster = 16;
 constexpr size_t kCounterBytes = kMaxTiles * sizeof(int);
 constexpr size_t kSmemLimitTwoCtas = 112 * 1024;  // M <= 8: two CTAs per SM
 constexpr size_t kSmemLimitOneCta = 220 * 1024;   // M > 8: one CTA per SM (register bound)
@@ -78,10 +75,9 @@ struct TmaGemvArgs {
   int splits;
   int x_stride;      // halves; == 8 mod 64 for conflict-free fragment reads
   int max_groups;
-  int spin;          // producer polls instead of sleeping on the empty barriers
 };
 
-template <int MT, bool CLUSTER>
+template <int MT>
 __global__ void __launch_bounds__(kThreads) __maxnreg__(MT == 1 ? 112 : 168) gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap,
                                                                const TmaGemvArgs a) {
   extern __shared__ unsigned char smem_raw[];
@@ -162,7 +158,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__(MT == 1 ? 112 : 168) gem
       int issued = prologue;
       for (int i = prologue; i < nst; ++i) {
         const int slot = i % kStages;
-        if (!mbar_wait(&empty[slot], ((i / kStages) - 1) & 1, &abort_flag, a.spin != 0)) break;
+        if (!mbar_wait(&empty[slot], ((i / kStages) - 1) & 1, &abort_flag, true)) break;
         issue(i, slot);
         ++issued;
       }
@@ -380,29 +376,6 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__(MT == 1 ? 112 : 168) gem
   }
   const bool failed = abort_flag != 0;
 
-  if (CLUSTER) {
-    // ---------------- split-K through DSMEM ----------------
-    cluster_sync();  // every CTA's partial is in its shared memory
-    if (!failed) {
-      const int S = a.splits;
-      const int c_lo = (split * kTileCols) / S, c_hi = ((split + 1) * kTileCols) / S;
-      const int width = c_hi - c_lo;
-      for (int i = threadIdx.x; i < a.M * width; i += kThreads) {
-        const int m = i / width, c = c_lo + i % width;
-        float part_q[kMaxCluster];
-#pragma unroll
-        for (int q = 0; q < kMaxCluster; ++q)
-          part_q[q] = q < S ? ld_shared_cluster_f32(map_shared_rank(red + m * kTileCols + c, q)) : 0.f;
-        float v = 0.f;
-#pragma unroll
-        for (int q = 0; q < kMaxCluster; ++q) v += part_q[q];  // fixed rank order
-        if (c < cols_valid) a.y[m * a.y_ld + col0 + c] = __float2half_rn(v);
-      }
-    }
-    cluster_sync();  // keep shared memory alive until every remote read is done
-    return;
-  }
-
   __syncthreads();
   if (threadIdx.x >= kTileCols) return;
   const int col = threadIdx.x;
@@ -441,43 +414,14 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__(MT == 1 ? 112 : 168) gem
 
 struct TmaPlan {
   int tiles, stages_total, splits, ks_max, x_stride, max_groups;
-  bool cluster;
   size_t smem, ws_bytes;
 };
-
-bool producer_spin_enabled() {
-  static const bool on = [] {
-    const char* e = std::getenv("ASHQK_GEMV_SPIN");
-    return !(e && e[0] == '0');
-  }();
-  return on;
-}
-
-int ctas_per_sm_target() {
-  static const int v = [] {
-    const char* e = std::getenv("ASHQK_GEMV_CTAS_PER_SM");
-    const int x = e ? std::atoi(e) : 0;
-    return x > 0 ? x : 1;
-  }();
-  return v;
-}
-
-// Split-K through thread-block clusters and DSMEM (env ASHQK_GEMV_CLUSTER=1)
-// or through workspace slots (default).
-bool use_cluster_reduction() {
-  static const bool on = [] {
-    const char* e = std::getenv("ASHQK_GEMV_CLUSTER");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
 
 void plan_tma(int M, int N, int K, int G, int split_req, int sm_count, TmaPlan* p) {
   p->tiles = ceil_div(N, kTileCols);
   p->stages_total = ceil_div(K, kStageRows);
-  int splits = split_req > 0 ? split_req
-                             : std::max(1, (ctas_per_sm_target() * sm_count + p->tiles / 2) / p->tiles);
-  if (split_req <= 0 && use_cluster_reduction()) splits = std::min(splits, kMaxCluster);
+  // Without a requested split: about one CTA per SM.
+  int splits = split_req > 0 ? split_req : std::max(1, (sm_count + p->tiles / 2) / p->tiles);
   splits = std::min(std::max(splits, 1), p->stages_total);
   // The split is a hint: raise it until the staged slice fits in shared memory.
   for (;; ++splits) {
@@ -490,24 +434,21 @@ void plan_tma(int M, int N, int K, int G, int split_req, int sm_count, TmaPlan* 
               static_cast<size_t>(p->max_groups) * kTileWords * 4 + (2 * kStages + 2) * 8;
     if (p->smem <= (M > 8 ? kSmemLimitOneCta : kSmemLimitTwoCtas) || splits >= p->stages_total) break;
   }
-  p->cluster = use_cluster_reduction() && p->splits > 1 && p->splits <= kMaxCluster;
-  p->ws_bytes = (p->splits > 1 && !p->cluster)
+  p->ws_bytes = p->splits > 1
                     ? kCounterBytes + static_cast<size_t>(p->tiles) * p->splits * M * kTileCols * 4
                     : 0;
 }
 
-template <int MT, bool CLUSTER>
+template <int MT>
 int launch_tma(const CUtensorMap& map, const TmaGemvArgs& args, const TmaPlan& p, cudaStream_t stream) {
   static std::atomic<bool> configured[64];  // zero-initialised (static storage)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ASHQK_ERR_CUDA;
-  auto kernel = gemv_tma_kernel<MT, CLUSTER>;
+  auto kernel = gemv_tma_kernel<MT>;
   if (!configured[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimitOneCta) != cudaSuccess ||
         cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared) != cudaSuccess)
-      return ASHQK_ERR_CUDA;
-    if (CLUSTER && cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
       return ASHQK_ERR_CUDA;
     configured[dev].store(true, std::memory_order_release);
   }
@@ -516,15 +457,8 @@ int launch_tma(const CUtensorMap& map, const TmaGemvArgs& args, const TmaPlan& p
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = p.smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[1];
   int n = 0;
-  if (CLUSTER) {
-    attr[n].id = cudaLaunchAttributeClusterDimension;
-    attr[n].val.clusterDim.x = 1;
-    attr[n].val.clusterDim.y = p.splits;
-    attr[n].val.clusterDim.z = 1;
-    ++n;
-  }
   if (pdl_enabled()) {
     attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[n].val.programmaticStreamSerializationAllowed = 1;
@@ -581,7 +515,6 @@ int gemv_tma_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw
   a.splits = p.splits;
   a.x_stride = p.x_stride;
   a.max_groups = p.max_groups;
-  a.spin = producer_spin_enabled() ? 1 : 0;
   if (p.ws_bytes > 0) {
     a.counters = static_cast<int*>(workspace);
     a.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
@@ -589,8 +522,7 @@ int gemv_tma_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw
     a.counters = nullptr;
     a.ws = nullptr;
   }
-  if (M > 8) return p.cluster ? launch_tma<2, true>(map, a, p, stream) : launch_tma<2, false>(map, a, p, stream);
-  return p.cluster ? launch_tma<1, true>(map, a, p, stream) : launch_tma<1, false>(map, a, p, stream);
+  return M > 8 ? launch_tma<2>(map, a, p, stream) : launch_tma<1>(map, a, p, stream);
 }
 
 }  // namespace ashqk

@@ -1,8 +1,9 @@
-"""Arithmetic of the column-strip GEMV's RAW variant, emulated in numpy (no GPU).
+"""Arithmetic of the decode GEMV's per-group zero-point correction, emulated in numpy (no GPU).
 
-The variant feeds the magic-number halves 1024 + q (low-nibble columns 0, 1, 4, 5 of a packed
-word) and 1024 + 16 q (high-nibble columns 2, 3, 6, 7) to the mma without subtracting the zero
-point, accumulates each group's sum of x with an mma against ones, and corrects once per group:
+The cluster-split kernel (csrc/gemv_cluster.cu) feeds the magic-number halves 1024 + q (low-nibble
+columns 0, 1, 4, 5 of a packed word) and 1024 + 16 q (high-nibble columns 2, 3, 6, 7) to the mma
+without subtracting the zero point, accumulates each group's sum of x with an mma against ones,
+and corrects once per group:
 
     sum x (q - z) = f * dot - (c + z) * sum x,   f = 1, c = 1024 (low);  f = 1/16, c = 64 (high)
 
@@ -30,7 +31,7 @@ def _unpacked(qw, qz):
 
 
 def _raw_gemv(x, qw, qz, s, g):
-    """The RAW kernel's arithmetic: returns fp16 y [M, N]."""
+    """The kernel's arithmetic (uncorrected mma, ones-mma, per-group correction): fp16 y [M, N]."""
     q, z = _unpacked(qw, qz)
     k, n = q.shape
     low = np.tile(LOW_COLS, n // 8)

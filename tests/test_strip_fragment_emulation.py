@@ -2,14 +2,12 @@
 
 Emulates, on the bytes of a shared-memory stage, exactly what each of a warp's 32 lanes loads and
 computes: the weight-row offsets, the byte permutes (``prmt``) and nibble masks that build the
-mma.sync A fragments, the x loads that build the B fragments, and -- for the PERM variant -- the
-per-stage rewrite of x (k permuted inside each 16-value block, 16-byte chunks rotated by token).
-The fragments of all lanes are then assembled into the m16n8k16 A (16 x 16) and B (16 x 8)
+mma.sync A fragments and the x loads that build the B fragments. The fragments of all lanes are then assembled into the m16n8k16 A (16 x 16) and B (16 x 8)
 matrices following the PTX fragment layout, multiplied, and compared with the dot products the
 kernel's epilogue assumes: row r of mma j is column j (r < 8) or j + 4 (r >= 8) of word r % 8,
-column n is token 8 * mt + n. Values are the RAW variant's magic-number halves (1024 + q for
-columns 0, 1, 4, 5 of a word, 1024 + 16 q for 2, 3, 6, 7); the nibble selection is the same in the
-zero-point-subtracting variant.
+column n is token 8 * mt + n. The fragments are checked on the magic-number halves (1024 + q for
+columns 0, 1, 4, 5 of a word, 1024 + 16 q for 2, 3, 6, 7) before the kernel subtracts the zero point,
+so the nibble selection is what is tested.
 """
 
 from __future__ import annotations
@@ -31,7 +29,7 @@ def lop3_and_or(v: int, mask: int, magic: int) -> int:
     return (v & mask) | magic
 
 
-def unpack_raw(T: int):
+def magic_halves(T: int):
     T8 = T >> 8
     return [lop3_and_or(T, 0x000F000F, 0x64006400), lop3_and_or(T, 0x00F000F0, 0x64006400),
             lop3_and_or(T8, 0x000F000F, 0x64006400), lop3_and_or(T8, 0x00F000F0, 0x64006400)]
@@ -58,29 +56,17 @@ class Stage:
         i = byte_off // 2
         return int(flat[i]) | (int(flat[i + 1]) << 16)
 
-    def x_prep(self):
-        """The PERM rewrite: lane l permutes chunk l of row m and stores it at chunk l ^ (m & 7)."""
-        for m in range(self.M):
-            row = self.x[m].copy()
-            chunks = row.view(np.uint32).reshape(32, 4)
-            out = np.empty_like(chunks)
-            for lane in range(32):
-                vx, vy, vz, vw = (int(c) for c in chunks[lane])
-                o = [prmt(vx, vz, 0x5410), prmt(vx, vz, 0x7632), prmt(vy, vw, 0x5410), prmt(vy, vw, 0x7632)]
-                out[lane ^ (m & 7)] = o
-            self.x[m] = out.reshape(-1).view(np.uint16)
 
-
-def emulate_step(stage: Stage, s: int, perm: bool, mt_count: int):
+def emulate_step(stage: Stage, s: int, mt_count: int):
     """Assemble, for every mma j and token tile mt, the A and B matrices the warp feeds mma.sync."""
     A = np.full((4, 16, 16), np.nan)
     B = np.full((mt_count, 16, 8), np.nan)
     for lane in range(32):
         g, t = lane >> 2, lane & 3
-        roff = [((t + 4 * q) if perm else (2 * t + (q & 1) + 8 * (q >> 1))) * 32 + 4 * g for q in range(4)]
+        roff = [(2 * t + (q & 1) + 8 * (q >> 1)) * 32 + 4 * g for q in range(4)]
         w = [stage.w_at(s * 16 * 32 + r) for r in roff]
-        oa, ob = unpack_raw(prmt(w[0], w[1], 0x6420)), unpack_raw(prmt(w[0], w[1], 0x7531))
-        oc, od = unpack_raw(prmt(w[2], w[3], 0x6420)), unpack_raw(prmt(w[2], w[3], 0x7531))
+        oa, ob = magic_halves(prmt(w[0], w[1], 0x6420)), magic_halves(prmt(w[0], w[1], 0x7531))
+        oc, od = magic_halves(prmt(w[2], w[3], 0x6420)), magic_halves(prmt(w[2], w[3], 0x7531))
         for j in range(4):
             sl = ((j & 1) << 1) | (j >> 1)
             regs = [oa[sl], ob[sl], oc[sl], od[sl]]
@@ -92,12 +78,8 @@ def emulate_step(stage: Stage, s: int, perm: bool, mt_count: int):
             b0 = b1 = 0
             if tok < stage.M:
                 xrow = tok * X_ROW_BYTES + 4 * t
-                if perm:
-                    b0 = stage.x_u32(xrow + (((2 * s) ^ g) << 4))
-                    b1 = stage.x_u32(xrow + (((2 * s + 1) ^ g) << 4))
-                else:
-                    b0 = stage.x_u32(xrow + s * 32)
-                    b1 = stage.x_u32(xrow + s * 32 + 16)
+                b0 = stage.x_u32(xrow + s * 32)
+                b1 = stage.x_u32(xrow + s * 32 + 16)
             for reg, kb in ((b0, 2 * t), (b1, 2 * t + 8)):
                 assert np.isnan(B[mt, kb, g])
                 B[mt, kb, g], B[mt, kb + 1, g] = halves(reg)
@@ -105,23 +87,20 @@ def emulate_step(stage: Stage, s: int, perm: bool, mt_count: int):
     return A, B
 
 
-@pytest.mark.parametrize("perm", [False, True])
 @pytest.mark.parametrize("m", [1, 4, 9, 16])
-def test_fragments_compute_the_strip_dot_products(perm, m):
-    rng = np.random.default_rng(1000 * m + perm)
+def test_fragments_compute_the_strip_dot_products(m):
+    rng = np.random.default_rng(1000 * m)
     k0, n_words = 0, 8
     q = rng.integers(0, 16, (256, 8 * n_words))
     words = O.pack_awq(q.astype(np.int32)).view(np.uint32)      # [256, 8]: the stage's weight box
     x = rng.standard_normal((m, 256)).astype(np.float16)
     stage = Stage(words, x)
-    if perm:
-        stage.x_prep()
     mt_count = 2 if m > 8 else 1
     low = np.array([c % 4 < 2 for c in range(8)])
     magic = np.where(np.tile(low, n_words), 1024 + q, 1024 + 16 * q).astype(np.float64)  # [256, 64]
     xf = x.astype(np.float64)
     for s in range(16):
-        A, B = emulate_step(stage, s, perm, mt_count)
+        A, B = emulate_step(stage, s, mt_count)
         for j in range(4):
             for mt in range(mt_count):
                 C = A[j] @ B[mt]                                  # [16 mma rows, 8 tokens]
@@ -131,94 +110,35 @@ def test_fragments_compute_the_strip_dot_products(perm, m):
                         tok = 8 * mt + n
                         want = 0.0 if tok >= m else float(magic[k0 + 16 * s:k0 + 16 * s + 16, col]
                                                             @ xf[tok, 16 * s:16 * s + 16])
-                        assert C[r, n] == pytest.approx(want, rel=1e-12, abs=1e-9), (perm, s, j, mt, r, n)
+                        assert C[r, n] == pytest.approx(want, rel=1e-12, abs=1e-9), (s, j, mt, r, n)
 
 
-def test_perm_reads_are_bank_conflict_free():
-    """Weight loads (per q) and x loads (per mt, for a full 8-token fragment) of the PERM variant
-    hit 32 distinct banks; the original order puts lanes t and t + 2 on the same banks."""
-    def banks(offsets):
-        return [(o // 4) % 32 for o in offsets]
-
-    for q in range(4):
-        perm = banks([(t + 4 * q) * 32 + 4 * g for g in range(8) for t in range(4)])
-        orig = banks([(2 * t + (q & 1) + 8 * (q >> 1)) * 32 + 4 * g for g in range(8) for t in range(4)])
-        assert len(set(perm)) == 32 and len(set(orig)) == 16
-    for s in range(16):
-        perm = banks([g * X_ROW_BYTES + 4 * t + (((2 * s) ^ g) << 4) for g in range(8) for t in range(4)])
-        orig = banks([g * X_ROW_BYTES + 4 * t + s * 32 for g in range(8) for t in range(4)])
-        assert len(set(perm)) == 32 and len(set(orig)) == 4
-
-
-NIBBLE_OF_COL = (0, 4, 1, 5, 2, 6, 3, 7)  # kAwqNibbleOfCol in csrc/awq_unpack.cuh
-
-
-@pytest.mark.parametrize("perm", [False, True])
-def test_raw_flush_recovers_q_minus_z(perm):
-    """The RAW epilogue per lane: C fragments of mma j scaled by f_j, minus (c + z) times the group's
-    sum of x taken from the ones-mma's c0 / c1, give sum x (q - z) for the lane's columns and tokens
-    (one group = one 16-row step here, zero points from the packed qzeros word of word g)."""
-    rng = np.random.default_rng(5 + perm)
-    m = 8
-    q = rng.integers(0, 16, (256, 64))
-    z = rng.integers(0, 16, (1, 64))
-    zwords = [int(w) for w in O.pack_awq(z.astype(np.int32)).view(np.uint32)[0]]
-    stage = Stage(O.pack_awq(q.astype(np.int32)).view(np.uint32), rng.standard_normal((m, 256)).astype(np.float16))
-    xf = stage.x.view(np.float16).astype(np.float64).copy()  # before the PERM rewrite
-    if perm:
-        stage.x_prep()
-    for s in (0, 7, 15):
-        A, B = emulate_step(stage, s, perm, 1)
-        ones = np.ones((16, 16))
-        SX = ones @ B[0]                                   # the ones-mma: every row holds sum_k x
-        for lane in range(32):
-            g, t = lane >> 2, lane & 3
-            zk = [((zwords[g] >> (4 * NIBBLE_OF_COL[c])) & 15) + (64.0 if c & 2 else 1024.0) for c in range(8)]
-            psx = (SX[g, 2 * t], SX[g, 2 * t + 1])         # c0, c1 of the ones-mma
-            for j in range(4):
-                f = 1.0 if j < 2 else 1 / 16
-                C = A[j] @ B[0]
-                frag = [(C[g, 2 * t], j, 0), (C[g, 2 * t + 1], j, 1), (C[g + 8, 2 * t], 4 + j, 0),
-                        (C[g + 8, 2 * t + 1], 4 + j, 1)]
-                for val, c, tsel in frag:
-                    got = val * f - zk[c] * psx[tsel]
-                    col, tok = 8 * g + c, 2 * t + tsel
-                    ks = slice(16 * s, 16 * s + 16)
-                    want = float(xf[tok, ks] @ (q[ks, col] - z[0, col]))
-                    assert got == pytest.approx(want, rel=1e-9, abs=1e-6), (perm, s, lane, j, c)
-
-
-def _consumer_strip(x, q, z, s_scales, g_size, raw, perm):
+def _consumer_strip(x, q, z, s_scales, g_size):
     """The consumer warp's whole K loop for one 64-column strip, lane by lane: per 16-row step the
     warp-wide mma on the assembled fragments (fp32 accumulation into the lanes' partials), a flush
-    at every quantization-group change (RAW: the per-group correction), and the final per-lane
+    at every quantization-group change, and the final per-lane
     accumulators mapped back to y[token, column] as the kernel's reduction stores them."""
     m, k = x.shape
     mt_count = 2 if m > 8 else 1
     words = O.pack_awq(q.astype(np.int32)).view(np.uint32)          # [K, 8]
-    zwords = O.pack_awq(z.astype(np.int32)).view(np.uint32)         # [K/G, 8]
     low = np.array([c % 4 < 2 for c in range(8)])
     acc = np.zeros((32, mt_count, 4, 4), np.float32)
     part = np.zeros_like(acc)
-    psx = np.zeros((32, mt_count, 4), np.float32)
     cur = -1
     for k0 in range(0, k, 256):
         stage = Stage(words[k0:k0 + 256], x[:, k0:k0 + 256])
-        if perm:
-            stage.x_prep()
         for s in range(min(256, k - k0) // 16):
             grp = (k0 + 16 * s) // g_size
             if grp != cur:
                 if cur >= 0:
-                    _flush(acc, part, psx, zwords[cur], s_scales[cur], raw)
+                    _flush(acc, part, s_scales[cur])
                 cur = grp
-            A, B = emulate_step(stage, s, perm, mt_count)
-            if not raw:  # the subtracting variant feeds (q - z): rebuild A from the magic values
-                zc = z[cur]
-                for j in range(4):
-                    for r in range(16):
-                        col = 8 * (r % 8) + j + (4 if r >= 8 else 0)
-                        A[j, r] = (A[j, r] - 1024) / (1 if low[col % 8] else 16) - zc[col]
+            A, B = emulate_step(stage, s, mt_count)
+            zc = z[cur]  # the kernel feeds (q - z): rebuild A from the magic values
+            for j in range(4):
+                for r in range(16):
+                    col = 8 * (r % 8) + j + (4 if r >= 8 else 0)
+                    A[j, r] = (A[j, r] - 1024) / (1 if low[col % 8] else 16) - zc[col]
             for lane in range(32):
                 g, t = lane >> 2, lane & 3
                 for mt in range(mt_count):
@@ -226,9 +146,7 @@ def _consumer_strip(x, q, z, s_scales, g_size, raw, perm):
                         C = (A[j].astype(np.float64) @ B[mt].astype(np.float64)).astype(np.float32)
                         part[lane, mt, j] += np.array([C[g, 2 * t], C[g, 2 * t + 1], C[g + 8, 2 * t],
                                                        C[g + 8, 2 * t + 1]], np.float32)
-                    sx = B[mt].sum(axis=0).astype(np.float32)           # the ones-mma, column n
-                    psx[lane, mt] += np.array([sx[2 * t], sx[2 * t + 1], 0, 0], np.float32)
-    _flush(acc, part, psx, zwords[cur], s_scales[cur], raw)
+    _flush(acc, part, s_scales[cur])
     y = np.zeros((m, 64), np.float32)
     for lane in range(32):
         g, t = lane >> 2, lane & 3
@@ -241,29 +159,20 @@ def _consumer_strip(x, q, z, s_scales, g_size, raw, perm):
     return y
 
 
-def _flush(acc, part, psx, zrow_words, srow, raw):
+def _flush(acc, part, srow):
     for lane in range(32):
         g = lane >> 2
-        zw = int(zrow_words[g])
-        zk = [((zw >> (4 * NIBBLE_OF_COL[c])) & 15) + (64.0 if c & 2 else 1024.0) for c in range(8)]
         sc = srow[8 * g:8 * g + 8].astype(np.float32)
         for mt in range(part.shape[1]):
             for j in range(4):
-                p = part[lane, mt, j].copy()
-                if raw:
-                    f = np.float32(1.0 if j < 2 else 1 / 16)
-                    p = p * f - np.array([zk[j] * psx[lane, mt, 0], zk[j] * psx[lane, mt, 1],
-                                          zk[4 + j] * psx[lane, mt, 0], zk[4 + j] * psx[lane, mt, 1]], np.float32)
-                acc[lane, mt, j] += np.array([sc[j], sc[j], sc[4 + j], sc[4 + j]], np.float32) * p
+                acc[lane, mt, j] += np.array([sc[j], sc[j], sc[4 + j], sc[4 + j]], np.float32) * part[lane, mt, j]
                 part[lane, mt, j] = 0
-            psx[lane, mt] = 0
 
 
 @pytest.mark.parametrize("g_size", [32, 64, 128])
 @pytest.mark.parametrize("m", [1, 9])
-@pytest.mark.parametrize("raw,perm", [(False, False), (True, False), (True, True)])
-def test_consumer_loop_matches_the_oracle(g_size, m, raw, perm):
-    """The strip consumer's K loop (two stages, several quantization groups) in each variant gives
+def test_consumer_loop_matches_the_oracle(g_size, m):
+    """The strip consumer's K loop (two stages, several quantization groups) gives
     y within the reference's parity criterion of the oracle's fp64 truth, on one 64-column strip."""
     rng = np.random.default_rng(g_size + 7 * m)
     k = 512
@@ -276,5 +185,5 @@ def test_consumer_loop_matches_the_oracle(g_size, m, raw, perm):
     w16 = O.dequantize_awq(qw, qz, s_scales, np.float16)
     e_fp16 = O.rel_err((x.astype(np.float32) @ w16.astype(np.float32)).astype(np.float16).astype(np.float32),
                        y_true)
-    y = _consumer_strip(x, q, z, s_scales, g_size, raw, perm).astype(np.float16).astype(np.float32)
+    y = _consumer_strip(x, q, z, s_scales, g_size).astype(np.float16).astype(np.float32)
     assert O.rel_err(y, y_true) <= 2 * e_fp16 + 1e-5, (O.rel_err(y, y_true), e_fp16)
