@@ -8,11 +8,11 @@
 // What bounds a streaming kernel on B200 (measured here): a TMA producer's
 // round -- wait for a free slot, arm its barrier, issue the copies -- costs
 // about 600-700 SM cycles plus about 100 per copy while copies are in flight,
-// whatever their size. A CTA that refills 4-9 KB per round therefore streams
-// only 5-10 bytes per cycle, a fraction of an SM's share of HBM (~22 B/cycle).
-// So every stage here carries 32 KB of packed weights (a 256-column tile: one
-// 256-row box; a 512-column tile: two 128-row boxes), with its x, scale and
-// zero rows: 4-6 copies per 33 KB round.
+// whatever their size, and one CTA's copies land at ~45 GB/s at most even from
+// L2. So every stage carries 32 KB of packed weights (a 256-column tile: one
+// 256-row box; a 512-column tile: two 128-row boxes) and its x, and nothing
+// else: the scale and zero rows of the CTA's whole K range come once, at the
+// start, in one or two copies each.
 //
 // Work split. A tile's K is cut into stages; a cluster of C CTAs owns one tile
 // and deals its stages out in C contiguous ranges. (tile width, C) is chosen per
@@ -62,6 +62,8 @@ constexpr int kBlockRows = 128;            // rows per consumer warp per stage
 constexpr int kStepBytes = 16 * 128;       // 16 rows of a 128-byte box row
 constexpr int kStageWeightBytes = 32768;   // packed weights per stage
 constexpr int kConsumers = 8;
+// A consumed stage holds the partial strips of all consumer warps (16 tokens at most) before they are sent.
+static_assert(kStageWeightBytes >= kConsumers * kStripCols * 16 * 4, "staging area");
 constexpr int kMaxRing = 8;
 constexpr int kMaxCluster = 16;
 
@@ -75,13 +77,20 @@ struct ClusterArgs {
   int stages;       // per tile: ceil(K / R)
   int C;            // CTAs per cluster (K split), == gridDim.x
   int ring;         // stages resident in shared memory
-  int gps;          // scale / zero rows loaded per stage
   int stage_bytes;  // multiple of 1024
-  int x_off, s_off, z_off;
+  int x_off;        // x within a stage
+  // Scale / zero area: scale rows [W / 256][sz_rows][256] fp16, then zero rows [sz_rows][W / 8] int32.
+  // hoisted: one area for the CTA's whole K range, loaded once (sz_off from the shared-memory base);
+  // otherwise one per stage with the rows of that stage's groups (sz_off from the stage's base).
+  int hoisted;
+  int sz_off;
+  int z_off;        // zero rows within the area
+  int sz_rows;      // rows the area holds: >= the groups its K range spans
+  int sz_box_rows;  // rows per copy
   int tile_off;     // byte offset of the CTA's partial tile (outside the ring)
-  int prefetch;     // stages prefetched into L2 ahead of the ring
   int y_pairs;      // y rows allow 4-byte half2 stores
-  uint32_t tx_bytes;
+  uint32_t tx_bytes;     // per stage: weights, x (and the area when not hoisted)
+  uint32_t sz_tx_bytes;  // a hoisted area
 };
 
 struct ClusterMaps {
@@ -124,28 +133,25 @@ __device__ __forceinline__ void cluster_arrive_release() {
 __device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 // Stores into another CTA's shared memory that complete on that CTA's mbarrier (bytes counted).
-__device__ __forceinline__ void st_async_f32(uint32_t remote_addr, float v, uint32_t remote_bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(remote_addr),
-               "r"(__float_as_uint(v)), "r"(remote_bar)
+__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, uint4 v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   remote_addr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(remote_bar)
                : "memory");
 }
-__device__ __forceinline__ void st_async_v2(uint32_t remote_addr, float v0, float v1, uint32_t remote_bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(
-                   remote_addr),
-               "r"(__float_as_uint(v0)), "r"(__float_as_uint(v1)), "r"(remote_bar)
+__device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
                : "memory");
+  return v;
 }
 __device__ __forceinline__ void sts_f32(uint32_t addr, float v) {
   asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 __device__ __forceinline__ void sts_f32x2(uint32_t addr, float v0, float v1) {
   asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(v0), "f"(v1) : "memory");
-}
-
-__device__ __forceinline__ void prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
 }
 
 // TOKS: 1 (M == 1), 8 (M <= 8) or 16 (M <= 16). GB: one quantization group per 128-row block
@@ -159,6 +165,7 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t full[kMaxRing];
   __shared__ uint64_t empty[kMaxRing];
+  __shared__ uint64_t sz_full;   // the CTA's scale and zero rows have landed
   __shared__ uint64_t partials;  // the other CTAs' partial strips for this CTA have arrived
   __shared__ int abort_flag;
 
@@ -181,6 +188,7 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kConsumers);
     }
+    mbar_init(&sz_full, 1);
     mbar_init(&partials, 1);
     if (C > 1 && my_strips > 0)  // what the other CTAs will store here with st.async
       mbar_arrive_expect_tx(&partials, static_cast<uint32_t>(my_strips * (C - 1) * blocks * kStripCols * M * 4));
@@ -208,40 +216,45 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
       prefetch_tensormap(&maps.z);
       const int boxes = W / 256;
       const int col_words = tile * (W / 8);
-      const int s_off = a.s_off, z_off = a.z_off, x_off = a.x_off, gps = a.gps, pf = a.prefetch;
+      const int x_off = a.x_off;
       const uint32_t tx = a.tx_bytes;
+      // Scale and zero rows from group g0 into the area at sz, completing on bar.
+      auto issue_sz = [&](unsigned char* sz, int g0, uint64_t* bar) {
+        for (int r = 0; r < a.sz_rows; r += a.sz_box_rows) {
+          for (int b = 0; b < boxes; ++b)
+            tma_load_2d(sz + (b * a.sz_rows + r) * 512, &maps.s, 8 * col_words + 256 * b, g0 + r, bar);
+          tma_load_2d(sz + a.z_off + r * (W / 2), &maps.z, col_words, g0 + r, bar);
+        }
+      };
+      if (a.hoisted) {  // every group this CTA's stages touch, before any stage
+        mbar_arrive_expect_tx(&sz_full, a.sz_tx_bytes);
+        issue_sz(smem + a.sz_off, st0 * R / G, &sz_full);
+      }
       auto issue_weights = [&](int li, int slot) {
         const int k0 = (st0 + li) * R;
         unsigned char* base = smem + slot * stage_bytes;
         mbar_arrive_expect_tx(&full[slot], tx);
-        for (int b = 0; b < boxes; ++b) {
-          tma_load_2d(base + b * R * 128, &maps.qw, col_words + 32 * b, k0, &full[slot]);
-          tma_load_2d(base + s_off + b * gps * 512, &maps.s, 8 * col_words + 256 * b, k0 / G, &full[slot]);
-        }
-        tma_load_2d(base + z_off, &maps.z, col_words, k0 / G, &full[slot]);
-      };
-      auto prefetch_weights = [&](int li) {  // into L2 only: the ring loads it later without DRAM latency
-        for (int b = 0; b < boxes; ++b) prefetch_l2_2d(&maps.qw, col_words + 32 * b, (st0 + li) * R);
+        for (int b = 0; b < boxes; ++b) tma_load_2d(base + b * R * 128, &maps.qw, col_words + 32 * b, k0, &full[slot]);
+        if (!a.hoisted) issue_sz(base + a.sz_off, k0 / G, &full[slot]);
       };
       auto issue_x = [&](int li, int slot) {
         tma_load_3d(smem + slot * stage_bytes + x_off, &maps.x, 0, 0, (st0 + li) * R / 16, &full[slot]);
       };
       const int prologue = min(nloc, ring);
       for (int li = 0; li < prologue; ++li) issue_weights(li, li);
-      for (int li = prologue; li < min(nloc, prologue + pf); ++li) prefetch_weights(li);
       pdl_wait();  // x is the previous kernel's output
       for (int li = 0; li < prologue; ++li) issue_x(li, li);
       int issued = prologue;
       for (int li = prologue; li < nloc; ++li) {
         const int slot = li % ring;
         if (!mbar_wait(&empty[slot], ((li / ring) - 1) & 1, &abort_flag, true)) break;
-        if (li + pf < nloc) prefetch_weights(li + pf);
         issue_weights(li, slot);
         issue_x(li, slot);
         ++issued;
       }
       if (abort_flag) {  // let every issued copy land before the CTA's shared memory is released
         int unused = 0;
+        if (a.hoisted) mbar_wait(&sz_full, 0, &unused);
         for (int slot = 0; slot < ring && slot < issued; ++slot)
           mbar_wait(&full[slot], ((issued - 1 - slot) / ring) & 1, &unused);
       }
@@ -275,9 +288,13 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
       return xbase + row * 32 + 16 * (xq_half ^ ((row >> 2) & 1));
     };
     const int x_off = a.x_off;
-    const uint32_t s_lane = static_cast<uint32_t>(a.s_off + (strip >> 2) * a.gps * 512 + (strip & 3) * 128);
-    const uint32_t z_lane = static_cast<uint32_t>(a.z_off + strip * 32);
+    // Scale row r of this strip's box: (strip / 4) * sz_rows + r rows of 512 bytes; zero row r: W / 2 bytes.
+    const uint32_t s_lane =
+        static_cast<uint32_t>(a.sz_off + (strip >> 2) * a.sz_rows * 512 + (strip & 3) * 128);
+    const uint32_t z_lane = static_cast<uint32_t>(a.sz_off + a.z_off + strip * 32);
     const int z_pitch = W / 2;
+    uint32_t sz_base = smem_s;     // the area holding the current stage's groups
+    int g_ref = st0 * R / G;       // the group in its row 0
 
     float part[MT][4][4], psx[MT][4];
 #pragma unroll
@@ -313,12 +330,12 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
       }
     };
 
-    // Scale and zero point of this lane's 8 columns for group slot gslot of the stage at `base`.
-    auto load_group = [&](uint32_t base, int gslot) {
-      const uint32_t srow = base + s_lane + gslot * 512;
+    // Scale and zero point of this lane's 8 columns for group g_ref + gslot.
+    auto load_group = [&](int gslot) {
+      const uint32_t srow = sz_base + s_lane + gslot * 512;
       const uint4 sa = lds_v4(srow + 16 * wA);
       const uint4 sb = lds_v4(srow + 16 * (4 + wA));
-      const uint32_t zrow = base + z_lane + gslot * z_pitch;
+      const uint32_t zrow = sz_base + z_lane + gslot * z_pitch;
       const uint32_t za = lds_u32(zrow + 4 * wA) >> (16 * hA);
       const uint32_t zb = lds_u32(zrow + 4 * (4 + wA)) >> (16 * hA);
       const uint32_t sav[4] = {sa.x, sa.y, sa.z, sa.w};
@@ -372,8 +389,8 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
     };
     // Whole-block groups (G % 128 == 0): fold the block's sums into acc with its group's scale and
     // zero point, read from the stage now (nothing to zero: the next block starts from zero).
-    auto fold_block = [&](uint32_t base, int gslot) {
-      load_group(base, gslot);
+    auto fold_block = [&](int gslot) {
+      load_group(gslot);
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -389,21 +406,26 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
 
     int cur_grp = -1;
     int grp_end = -1;
-    auto enter_group = [&](uint32_t base, int k, int gbase) {
+    auto enter_group = [&](int k) {
       if (k >= grp_end) {  // a new quantization group (rows past K read zero scales: no effect)
         if (cur_grp >= 0) flush();
         cur_grp = k / G;
         grp_end = (cur_grp + 1) * G;
-        load_group(base, cur_grp - gbase);
+        load_group(cur_grp - g_ref);
       }
     };
-    for (int li = 0; li < nloc; ++li) {
+    // A hoisted scale / zero area is complete before the first group is read.
+    const bool sz_ok = !a.hoisted || mbar_wait(&sz_full, 0, &abort_flag, true);
+    for (int li = 0; sz_ok && li < nloc; ++li) {
       const int slot = li % ring;
       if (!mbar_wait(&full[slot], (li / ring) & 1, &abort_flag, true)) break;
       const uint32_t base = smem_s + slot * stage_bytes;
       const int k0 = (st0 + li) * R;
       const int kb = k0 + block * kBlockRows;
-      const int gbase = k0 / G;
+      if (!a.hoisted) {
+        sz_base = base;
+        g_ref = k0 / G;
+      }
       const uint32_t wbase = base + w_lane;
       const uint32_t xbase = base + x_off;
       // Loads run one step pair ahead of the arithmetic.
@@ -421,9 +443,9 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
           ldsm_x4_trans(wbase + (s + 2) * kStepBytes, Ran);
           ldsm_x4_trans(wbase + (s + 3) * kStepBytes, Rbn);
         }
-        if (!GB) enter_group(base, kb + 16 * s, gbase);
+        if (!GB) enter_group(kb + 16 * s);
         step(Ra, bx, 0, GB && s == 0);
-        if (!GB) enter_group(base, kb + 16 * (s + 1), gbase);
+        if (!GB) enter_group(kb + 16 * (s + 1));
         step(Rb, bx, 1, false);
         if (s + 2 < kBlockRows / 16) {
 #pragma unroll
@@ -435,7 +457,7 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
           }
         }
       }
-      if (GB) fold_block(base, kb / G - gbase);
+      if (GB) fold_block(kb / G - g_ref);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
@@ -443,11 +465,12 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
   }
 
   // ---------------- the cluster's sum ----------------
-  // Strip s of the tile is stored by CTA s % C of the cluster. Each consumer warp (strip, block) sends
-  // its partial strip straight from registers to that CTA's slot [rank * blocks + block] (st.async,
-  // completing on the owner's `partials` barrier; a plain store for its own strips); the owner adds
-  // the C * blocks slots in that fixed order and stores y. Slot layout [64 columns][M tokens] fp32,
-  // so a lane's two tokens of a column are one 8-byte store.
+  // Strip s of the tile is stored by CTA s % C of the cluster. Each consumer warp (strip, block) hands
+  // its partial strip to that CTA's slot [rank * blocks + block]; the owner adds the C * blocks slots in
+  // that fixed order and stores y. Slot layout [64 columns][M tokens] fp32. A strip owned here is
+  // stored straight from registers; one owned elsewhere is first laid out in this CTA's (consumed)
+  // ring and then sent as 16-byte st.async pieces, which complete on the owner's `partials` barrier --
+  // a quarter of the remote stores of sending single values.
   if (C > 1) cluster_wait_acquire();  // every CTA's `partials` barrier is armed
   if (warp < kConsumers) {
     const int strip = warp % strips, block = warp / strips;
@@ -457,8 +480,10 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
     // this strip's slot in the owner: owned strip index strip / C
     const uint32_t slot_base = static_cast<uint32_t>(((strip / C) * nsend + sender) * kStripCols * M * 4);
     const bool remote = owner != rank;
-    const uint32_t dst = remote ? map_shared_rank(slots, owner) + slot_base : smem_u32(slots) + slot_base;
-    const uint32_t bar = remote ? map_shared_rank(&partials, owner) : 0u;
+    // Every consumer warp is past its last stage before any of them reuses the ring.
+    if (C > 1) asm volatile("bar.sync 1, %0;" ::"r"(32 * kConsumers) : "memory");
+    const uint32_t dst = remote ? smem_u32(smem) + static_cast<uint32_t>(warp * kStripCols * M * 4)
+                                : smem_u32(slots) + slot_base;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -470,25 +495,18 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
           const uint32_t addr = dst + static_cast<uint32_t>((c * M + m0) * 4);
           const float v0 = acc[mt][j][2 * hh], v1 = acc[mt][j][2 * hh + 1];
           if (TOKS > 1 && m0 + 1 < M && (M & 1) == 0) {  // an 8-byte aligned pair of tokens
-            if (remote)
-              st_async_v2(addr, v0, v1, bar);
-            else
-              sts_f32x2(addr, v0, v1);
+            sts_f32x2(addr, v0, v1);
           } else {
-            if (m0 < M) {
-              if (remote)
-                st_async_f32(addr, v0, bar);
-              else
-                sts_f32(addr, v0);
-            }
-            if (TOKS > 1 && m0 + 1 < M) {
-              if (remote)
-                st_async_f32(addr + 4, v1, bar);
-              else
-                sts_f32(addr + 4, v1);
-            }
+            if (m0 < M) sts_f32(addr, v0);
+            if (TOKS > 1 && m0 + 1 < M) sts_f32(addr + 4, v1);
           }
         }
+    if (remote) {
+      __syncwarp();
+      const uint32_t rdst = map_shared_rank(slots, owner) + slot_base;
+      const uint32_t bar = map_shared_rank(&partials, owner);
+      for (int i = lane; i < kStripCols * M / 4; i += 32) st_async_v4(rdst + 16 * i, lds_v4(dst + 16 * i), bar);
+    }
   }
   __syncthreads();  // this CTA's own strips are in its slots
   bool failed = abort_flag != 0;
@@ -517,8 +535,9 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
 // ---------------------------------------------------------------------------
 
 struct ClusterPlan {
-  int W, R, tiles, stages, C, ctas, per, ring, gps, stage_bytes, x_off, s_off, z_off, tile_off, prefetch, toks;
-  uint32_t tx;
+  int W, R, tiles, stages, C, ctas, per, ring, stage_bytes, x_off, hoisted, sz_off, z_off, sz_rows, sz_box_rows,
+      tile_off, toks;
+  uint32_t tx, sz_tx;
   size_t smem;
 };
 
@@ -529,15 +548,14 @@ std::atomic<int> g_smem_kb{0};
 std::atomic<int> g_force_c{0};
 std::atomic<int> g_force_w{0};
 std::atomic<int> g_max_ctas{0};
-std::atomic<int> g_prefetch{-1};
 
 int align_to(int v, int a) { return (v + a - 1) / a * a; }
 
-// Scale / zero rows a stage of `rows` rows starting on a multiple of `rows` can span.
-int groups_per_stage(int rows, int G) {
-  if (rows % G == 0) return rows / G;
-  if (G % rows == 0) return 1;
-  return rows / G + 2;
+// Quantization groups that `stages` consecutive stages of R rows (starting on a stage boundary) span.
+int groups_spanned(int stages, int R, int G) {
+  if (R % G == 0) return stages * R / G;
+  if (stages == 1 && G % R == 0) return 1;
+  return (stages * R + G - 1) / G + 1;
 }
 
 }  // namespace
@@ -548,7 +566,8 @@ bool plan_cluster(int M, int N, int K, int G, int sm_count, ClusterPlan* p) {
   const int smem_kb = g_smem_kb.load(std::memory_order_relaxed);
   // M <= 8: two CTAs (this launch's and the next one's) per SM, 2 x (dynamic + ~0.5 KB static + 1 KB
   // reserved) within the SM's 228 KB; M > 8 needs the register file of a whole SM.
-  const size_t budget = smem_kb > 0 ? static_cast<size_t>(smem_kb) * 1024 : (M <= 8 ? 112 : 200) * 1024;
+  // Small quantization groups make the scale / zero area large: when nothing fits two per SM, one per SM.
+  const size_t budget0 = smem_kb > 0 ? static_cast<size_t>(smem_kb) * 1024 : (M <= 8 ? 112 : 200) * 1024;
   // Grid cap (measured on B200). M <= 8: up to ~1.65 CTAs per SM -- an SM that holds two CTAs of the
   // launch runs 16 consumer warps and gets through its stages ~1.7x faster than with one, while more
   // than ~1.65 per SM leaves clusters that cannot be placed with the others (a second wave). M > 8:
@@ -567,53 +586,77 @@ bool plan_cluster(int M, int N, int K, int G, int sm_count, ClusterPlan* p) {
   bool found = false;
   double best_cost = 0.0;
   int best_key[3] = {0, 0, 0};
-  for (int W : {256, 512}) {
-    if (force_w && W != force_w) continue;
-    ClusterPlan q;
-    q.toks = toks;
-    q.W = W;
-    q.R = kStageWeightBytes * 2 / W;
-    q.tiles = ceil_div(N, W);
-    q.stages = ceil_div(K, q.R);
-    q.gps = groups_per_stage(q.R, G);
-    if (q.gps > 256) continue;
-    q.x_off = kStageWeightBytes;
-    q.s_off = q.x_off + align_to(2 * q.R * M, 128);
-    q.z_off = q.s_off + (W / 256) * q.gps * 512;
-    q.stage_bytes = align_to(q.z_off + align_to(q.gps * W / 2, 128), 1024);
-    q.tx = static_cast<uint32_t>(kStageWeightBytes + 2 * q.R * M + (W / 256) * q.gps * 512 + q.gps * W / 2);
-    for (int C = 1; C <= kMaxCluster; ++C) {
-      if (force_c && C != force_c) continue;
-      if (C > q.stages) break;
-      q.C = C;
-      q.ctas = q.tiles * C;
-      if (q.ctas > max_ctas && !(force_c || (C == 1 && q.tiles > max_ctas))) continue;
-      q.per = ceil_div(q.stages, C);
-      // The partial strips this CTA stores: [ceil(strips / C)][C * blocks][64][M] fp32.
-      const int strips = W / kStripCols, blocks = kConsumers / strips;
-      const size_t slots = static_cast<size_t>(ceil_div(strips, C)) * C * blocks * kStripCols * M * 4;
-      if (slots + 1024 + q.stage_bytes > budget) continue;
-      int ring = static_cast<int>((budget - 1024 - slots) / q.stage_bytes);
-      ring = std::min(std::min(ring, kMaxRing), q.per);
-      if (ring < 1 || (ring < 2 && q.per > 1)) continue;
-      q.ring = ring;
-      q.tile_off = ring * q.stage_bytes;
-      q.smem = 1024 + static_cast<size_t>(q.tile_off) + slots;
-      const int pf = g_prefetch.load(std::memory_order_relaxed);
-      q.prefetch = q.per > ring ? (pf >= 0 ? pf : 4) : 0;
-      const double cost = M <= 8 ? q.per * (q.ctas > sm_count ? 1.18 : 1.0) + (C > 8 ? 0.5 : 0.0)
-                                 : static_cast<double>(q.per + C);
-      // ties: the 256-column tile (fewer copies per stage), then smaller clusters
-      const int key[3] = {W == 256 ? 0 : 1, C, 0};
-      if (!found || cost < best_cost - 1e-9 ||
-          (cost < best_cost + 1e-9 && std::lexicographical_compare(key, key + 3, best_key, best_key + 3))) {
-        found = true;
-        best_cost = cost;
-        std::copy(key, key + 3, best_key);
-        *p = q;
+  auto search = [&](size_t budget, int cta_cap) {
+    for (int W : {256, 512}) {
+      if (force_w && W != force_w) continue;
+      for (int hoisted = 1; hoisted >= 0; --hoisted) {
+        ClusterPlan q;
+        q.toks = toks;
+        q.W = W;
+        q.R = kStageWeightBytes * 2 / W;
+        q.tiles = ceil_div(N, W);
+        q.stages = ceil_div(K, q.R);
+        q.x_off = kStageWeightBytes;
+        q.hoisted = hoisted;
+        const int sz_row_bytes = (W / 256) * 512 + W / 2;
+        for (int C = 1; C <= kMaxCluster; ++C) {
+          if (force_c && C != force_c) continue;
+          if (C > q.stages) break;
+          q.C = C;
+          q.ctas = q.tiles * C;
+          if (q.ctas > cta_cap && !(force_c || (C == 1 && q.tiles > cta_cap))) continue;
+          q.per = ceil_div(q.stages, C);
+          // The partial strips this CTA stores: [ceil(strips / C)][C * blocks][64][M] fp32.
+          const int strips = W / kStripCols, blocks = kConsumers / strips;
+          const size_t slots = static_cast<size_t>(ceil_div(strips, C)) * C * blocks * kStripCols * M * 4;
+          // The scale / zero area: the groups of the longest stage range (hoisted) or of one stage, in
+          // copies of at most 256 rows.
+          const int span = groups_spanned(hoisted ? q.per : 1, q.R, G);
+          const int nbox = ceil_div(span, 256);
+          q.sz_box_rows = ceil_div(span, nbox);
+          q.sz_rows = nbox * q.sz_box_rows;
+          q.z_off = (W / 256) * q.sz_rows * 512;
+          const int sz_bytes = q.sz_rows * sz_row_bytes;
+          size_t hoisted_bytes = 0;
+          if (hoisted) {
+            q.stage_bytes = align_to(q.x_off + align_to(2 * q.R * M, 128), 1024);
+            q.tx = static_cast<uint32_t>(kStageWeightBytes + 2 * q.R * M);
+            q.sz_tx = static_cast<uint32_t>(sz_bytes);
+            hoisted_bytes = static_cast<size_t>(align_to(sz_bytes, 1024));
+          } else {
+            q.sz_off = q.x_off + align_to(2 * q.R * M, 128);
+            q.stage_bytes = align_to(q.sz_off + sz_bytes, 1024);
+            q.tx = static_cast<uint32_t>(kStageWeightBytes + 2 * q.R * M + sz_bytes);
+            q.sz_tx = 0;
+          }
+          if (slots + hoisted_bytes + 1024 + q.stage_bytes > budget) continue;
+          int ring = static_cast<int>((budget - 1024 - slots - hoisted_bytes) / q.stage_bytes);
+          ring = std::min(std::min(ring, kMaxRing), q.per);
+          if (ring < 1 || (ring < 2 && q.per > 1)) continue;
+          q.ring = ring;
+          if (hoisted) q.sz_off = ring * q.stage_bytes;
+          q.tile_off = ring * q.stage_bytes + static_cast<int>(hoisted_bytes);
+          q.smem = 1024 + static_cast<size_t>(q.tile_off) + slots;
+          // Per-stage scale / zero copies cost ~3% over a hoisted area (measured on the decode shapes).
+          const double cost = (M <= 8 ? q.per * (q.ctas > sm_count ? 1.18 : 1.0) + (C > 8 ? 0.5 : 0.0)
+                                      : static_cast<double>(q.per + C)) *
+                              (hoisted ? 1.0 : 1.03);
+          // ties: the 256-column tile (fewer copies per stage), then smaller clusters
+          const int key[3] = {W == 256 ? 0 : 1, C, 0};
+          if (!found || cost < best_cost - 1e-9 ||
+              (cost < best_cost + 1e-9 && std::lexicographical_compare(key, key + 3, best_key, best_key + 3))) {
+            found = true;
+            best_cost = cost;
+            std::copy(key, key + 3, best_key);
+            *p = q;
+          }
+        }
       }
     }
-  }
+  };
+  search(budget0, max_ctas);
+  if (!found && smem_kb == 0 && budget0 < 200 * 1024) search(200 * 1024, std::min(max_ctas, sm_count));
+  if (!found && smem_kb == 0 && budget0 < 200 * 1024) search(200 * 1024, max_ctas);
   return found;
 }
 
@@ -697,7 +740,7 @@ int gemv_cluster_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K / G)};
     const uint64_t strides[1] = {static_cast<uint64_t>(s_ld) * 2};
-    const uint32_t box[2] = {256, static_cast<uint32_t>(p.gps)};
+    const uint32_t box[2] = {256, static_cast<uint32_t>(p.sz_box_rows)};
     int rc = encode_tensor_map(&maps.s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(s), dims, strides,
                                box, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
@@ -705,7 +748,7 @@ int gemv_cluster_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(N / 8), static_cast<uint64_t>(K / G)};
     const uint64_t strides[1] = {static_cast<uint64_t>(qz_ld) * 4};
-    const uint32_t box[2] = {static_cast<uint32_t>(p.W / 8), static_cast<uint32_t>(p.gps)};
+    const uint32_t box[2] = {static_cast<uint32_t>(p.W / 8), static_cast<uint32_t>(p.sz_box_rows)};
     int rc = encode_tensor_map(&maps.z, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<int32_t*>(qz), dims, strides,
                                box, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
@@ -723,15 +766,17 @@ int gemv_cluster_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_
   a.stages = p.stages;
   a.C = p.C;
   a.ring = p.ring;
-  a.gps = p.gps;
   a.stage_bytes = p.stage_bytes;
   a.x_off = p.x_off;
-  a.s_off = p.s_off;
+  a.hoisted = p.hoisted;
+  a.sz_off = p.sz_off;
   a.z_off = p.z_off;
+  a.sz_rows = p.sz_rows;
+  a.sz_box_rows = p.sz_box_rows;
   a.tile_off = p.tile_off;
-  a.prefetch = p.prefetch;
   a.y_pairs = aligned(y, 4) && (y_ld % 2 == 0);
   a.tx_bytes = p.tx;
+  a.sz_tx_bytes = p.sz_tx;
   const bool gb = G % kBlockRows == 0;
   switch (p.toks) {
     case 1:
@@ -746,16 +791,14 @@ int gemv_cluster_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_
 
 }  // namespace ashqk
 
-extern "C" int ashqk_gemv_set_tuning(int smem_kb, int cluster_ctas, int tile_cols, int max_ctas, int prefetch_stages) {
+extern "C" int ashqk_gemv_set_tuning(int smem_kb, int cluster_ctas, int tile_cols, int max_ctas) {
   if (smem_kb < 0 || smem_kb > 200 || cluster_ctas < 0 || cluster_ctas > ashqk::kMaxCluster ||
-      (tile_cols != 0 && tile_cols != 256 && tile_cols != 512) || max_ctas < 0 || prefetch_stages < -1 ||
-      prefetch_stages > 16)
+      (tile_cols != 0 && tile_cols != 256 && tile_cols != 512) || max_ctas < 0)
     return ASHQK_ERR_INVALID_ARGUMENT;
   ashqk::g_smem_kb.store(smem_kb);
   ashqk::g_force_c.store(cluster_ctas);
   ashqk::g_force_w.store(tile_cols);
   ashqk::g_max_ctas.store(max_ctas);
-  ashqk::g_prefetch.store(prefetch_stages);
   return ASHQK_OK;
 }
 

@@ -365,7 +365,7 @@ def per_layer_gemv(stack, m, torch, reps=3):
         torch.cuda.synchronize()
         us = start.elapsed_time(end) * 1e3 / (reps * len(stack))
         nbytes = w4a16_bytes(m, n, k, GROUP)
-        res[name] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1), "launch": strip_plan(m, n, k)}
+        res[name] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1), "launch": cluster_plan(m, n, k)}
         del g
     return res
 
@@ -421,23 +421,24 @@ def decode_sweep(stack, torch, hbm_peak, reps=5):
     return out
 
 
-def strip_plan(m, n, k):
-    """The column-strip GEMV's launch shape for this layer on this device (ashqk_gemv_strip_plan)."""
+def cluster_plan(m, n, k):
+    """The cluster-split GEMV's launch shape for this layer on this device (ashqk_gemv_cluster_plan)."""
     import ctypes
 
     from ashqk import _ext
 
     class Plan(ctypes.Structure):
-        _fields_ = [(f, ctypes.c_int) for f in ("grid_x", "grid_y", "threads", "consumer_warps", "ring_stages",
-                                                "stages_total", "stage_bytes", "smem_bytes")]
+        _fields_ = [(f, ctypes.c_int) for f in ("tile_cols", "stage_rows", "tiles", "stages_per_tile", "cluster_ctas",
+                                                "ctas", "max_stages_per_cta", "threads", "ring_stages",
+                                                "stage_bytes", "smem_bytes")]
 
     lib = ctypes.CDLL(_ext.C_LIBRARY)
-    lib.ashqk_gemv_strip_plan.argtypes = [ctypes.c_int] * 5 + [ctypes.POINTER(Plan)]
+    lib.ashqk_gemv_cluster_plan.argtypes = [ctypes.c_int] * 5 + [ctypes.POINTER(Plan)]
     p = Plan()
-    if lib.ashqk_gemv_strip_plan(m, n, k, GROUP, 0, ctypes.byref(p)) != 0:
+    if lib.ashqk_gemv_cluster_plan(m, n, k, GROUP, 0, ctypes.byref(p)) != 0:
         return None
-    return {"grid": [p.grid_x, p.grid_y], "threads": p.threads, "ring_stages": p.ring_stages,
-            "smem_kb": round(p.smem_bytes / 1024, 1)}
+    return {"tile_cols": p.tile_cols, "cluster": p.cluster_ctas, "ctas": p.ctas,
+            "stages_per_cta": p.max_stages_per_cta, "ring": p.ring_stages, "smem_kb": round(p.smem_bytes / 1024, 1)}
 
 
 def cublas_fp16_stack(stack, steps, warmup, torch):

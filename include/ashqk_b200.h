@@ -248,12 +248,10 @@ ASHQK_API int ashqk_gemv_cluster_plan(int M, int N, int K, int group_size, int s
 /*
  * Tuning of the cluster-split decode GEMV's plan for later calls in this
  * process (0 = automatic for each): shared-memory budget per CTA in KiB
- * (32-200), CTAs per cluster (1-16), tile columns (256 or 512), a cap on the
- * grid's CTAs, and the stages of packed weights prefetched into L2 ahead of
- * the shared-memory ring (-1 = automatic, 0-16). No reference counterpart: a
- * benchmark sweep switch.
+ * (32-200), CTAs per cluster (1-16), tile columns (256 or 512) and a cap on
+ * the grid's CTAs. No reference counterpart: a benchmark sweep switch.
  */
-ASHQK_API int ashqk_gemv_set_tuning(int smem_kb, int cluster_ctas, int tile_cols, int max_ctas, int prefetch_stages);
+ASHQK_API int ashqk_gemv_set_tuning(int smem_kb, int cluster_ctas, int tile_cols, int max_ctas);
 
 /*
  * One-shot all-reduce of fp16 tensors over NVLink peer memory, for the

@@ -71,10 +71,10 @@ def test_kernel_switches_validate_their_argument(lib):
     for which in (0, 1, 2, 3, 4):
         assert lib.ashqk_set_gemv_kernel(which) == 0
     assert lib.ashqk_set_gemv_kernel(5) == 1 and lib.ashqk_set_gemv_kernel(-1) == 1
-    assert lib.ashqk_gemv_set_tuning(0, 0, 0, 0, -1) == 0 and lib.ashqk_gemv_set_tuning(96, 3, 512, 140, 2) == 0
-    assert lib.ashqk_gemv_set_tuning(-1, 0, 0, 0, -1) == 1 and lib.ashqk_gemv_set_tuning(0, 17, 0, 0, -1) == 1
-    assert lib.ashqk_gemv_set_tuning(0, 0, 128, 0, -1) == 1 and lib.ashqk_gemv_set_tuning(0, 0, 0, 0, -2) == 1
-    assert lib.ashqk_gemv_set_tuning(0, 0, 0, 0, -1) == 0
+    assert lib.ashqk_gemv_set_tuning(0, 0, 0, 0) == 0 and lib.ashqk_gemv_set_tuning(96, 3, 512, 140) == 0
+    assert lib.ashqk_gemv_set_tuning(-1, 0, 0, 0) == 1 and lib.ashqk_gemv_set_tuning(0, 17, 0, 0) == 1
+    assert lib.ashqk_gemv_set_tuning(0, 0, 128, 0) == 1 and lib.ashqk_gemv_set_tuning(0, 0, 0, -1) == 1
+    assert lib.ashqk_gemv_set_tuning(0, 0, 0, 0) == 0
     for which in (0, 1, 2, 3, 4):
         assert lib.ashqk_set_gemm_kernel(which) == 0
     assert lib.ashqk_set_gemm_kernel(5) == 1 and lib.ashqk_set_gemm_kernel(-1) == 1
@@ -258,7 +258,8 @@ def _cluster_plan(lib, m, n, k, g, sms):
 def test_cluster_plan_invariants(lib, sms):
     """The cluster-split GEMV's plan over decode shapes and every M: 32 KB of packed weights per stage,
     clusters of at most 16 CTAs, at most ~1.65 CTAs per SM for M <= 8 (~0.65 for M > 8) unless the
-    tiles alone exceed that, two CTAs' shared memory within an SM for M <= 8, a ring of at least two
+    tiles alone exceed that, two CTAs' shared memory within an SM for M <= 8 at the BASELINE group size
+    (smaller groups may need one CTA's worth for their scale / zero rows), a ring of at least two
     stages when a CTA has two, and the busiest CTA's stages the even share of its tile."""
     for n, k in _SHAPES:
         for g in (32, 64, 128):
@@ -267,6 +268,11 @@ def test_cluster_plan_invariants(lib, sms):
             for m in range(1, 17):
                 rc, p = _cluster_plan(lib, m, n, k, g, sms)
                 where = (m, n, k, g, sms)
+                if g < 128 and rc == 2:
+                    # A CTA keeps the scale / zero rows of its whole K range in shared memory; deep
+                    # layers with small groups on few CTAs do not fit and take the column-strip kernel.
+                    assert k >= 8192 and (m > 8 or sms < 100), where
+                    continue
                 assert rc == 0, where
                 assert p.tile_cols in (256, 512) and p.tile_cols * p.stage_rows // 2 == 32768, where
                 assert p.tiles == -(-n // p.tile_cols) and p.stages_per_tile == -(-k // p.stage_rows), where
@@ -278,10 +284,9 @@ def test_cluster_plan_invariants(lib, sms):
                 assert p.threads == 288 and 1 <= p.ring_stages <= min(8, p.max_stages_per_cta), where
                 assert p.ring_stages >= 2 or p.max_stages_per_cta == 1, where
                 assert p.stage_bytes % 1024 == 0 and p.ring_stages * p.stage_bytes + 1024 <= p.smem_bytes, where
-                if m <= 8:
+                assert p.smem_bytes <= 201 * 1024, where
+                if m <= 8 and g == 128:
                     assert 2 * (p.smem_bytes + 516 + 1024) <= 228 * 1024, where
-                else:
-                    assert p.smem_bytes <= 201 * 1024, where
 
 
 def test_cluster_plan_rejects(lib):

@@ -32,7 +32,7 @@ def lib():
     assert lib.ashqk_set_gemv_kernel(4) == 0
     yield lib
     assert lib.ashqk_set_gemv_kernel(0) == 0
-    assert lib.ashqk_gemv_set_tuning(0, 0, 0, 0, -1) == 0
+    assert lib.ashqk_gemv_set_tuning(0, 0, 0, 0) == 0
 
 
 def _check(x, qw, qz, s, y):
@@ -43,15 +43,16 @@ def _check(x, qw, qz, s, y):
     assert e <= 2 * e_cublas + 1e-5, (e, e_cublas)
 
 
-# (smem_kb, cluster CTAs, tile columns, max CTAs, L2 prefetch stages); 0 / -1 = automatic
-TUNINGS = [(0, 0, 0, 0, -1), (0, 1, 256, 0, -1), (0, 3, 512, 0, 0), (0, 5, 256, 0, 2), (0, 16, 256, 0, -1),
-           (0, 7, 512, 0, 8), (48, 2, 512, 0, -1), (0, 0, 0, 7, 1)]
+# (smem_kb, cluster CTAs, tile columns, max CTAs); 0 = automatic
+TUNINGS = [(0, 0, 0, 0), (0, 1, 256, 0), (0, 3, 512, 0), (0, 5, 256, 0), (0, 16, 256, 0), (0, 7, 512, 0),
+           (48, 2, 512, 0), (0, 0, 0, 7), (0, 1, 512, 0)]
 
 
-@pytest.mark.parametrize("tuning", TUNINGS, ids=[f"smem{a}-c{b}-w{c}-max{d}-pf{e}" for a, b, c, d, e in TUNINGS])
+@pytest.mark.parametrize("tuning", TUNINGS, ids=[f"smem{a}-c{b}-w{c}-max{d}" for a, b, c, d in TUNINGS])
 @pytest.mark.parametrize("m,n,k,g", [(1, 6144, 4096, 128), (1, 4096, 12288, 128), (4, 4096, 4096, 128),
                                      (3, 1024, 1152, 64), (8, 768, 640, 32), (13, 2048, 1024, 128),
-                                     (16, 512, 2048, 256), (2, 96, 4096, 128), (1, 64, 4096, 16)])
+                                     (16, 512, 2048, 256), (2, 96, 4096, 128), (1, 64, 4096, 16),
+                                     (13, 256, 8192, 64), (5, 512, 3072, 256)])
 def test_cluster_gemv_matches_oracle(lib, tuning, m, n, k, g):
     from ashqk import w4a16_linear
 
@@ -66,7 +67,7 @@ def test_cluster_gemv_matches_oracle(lib, tuning, m, n, k, g):
         _check(x, qw, qz, s, y)
         assert torch.equal(w4a16_linear(xd, qwd, qzd, sd), y)  # fixed summation order
     finally:
-        assert lib.ashqk_gemv_set_tuning(0, 0, 0, 0, -1) == 0
+        assert lib.ashqk_gemv_set_tuning(0, 0, 0, 0) == 0
 
 
 @pytest.mark.parametrize("m", [1, 2, 4, 8, 16])
