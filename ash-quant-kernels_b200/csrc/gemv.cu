@@ -384,7 +384,7 @@ bool gemv_cluster_eligible(const void* x, int64_t x_ld, const int32_t* qw, int64
                            int64_t qz_ld, const void* s, int64_t s_ld, int M, int N, int G);
 int gemv_cluster_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
                         int64_t qz_ld, const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K,
-                        int G, int sm_count, cudaStream_t stream);
+                        int G, int split, int sm_count, cudaStream_t stream);
 
 namespace {
 // 0 auto (cluster-split strips, then split-K TMA, then register streaming),
@@ -404,11 +404,11 @@ int gemv_workspace_bytes(int M, int N, int K, int G, int split_k, size_t* bytes)
   return ASHQK_OK;
 }
 
-bool gemv_cluster_plannable(int M, int N, int K, int G, int sm_count);
+bool gemv_cluster_plannable(int M, int N, int K, int G, int sm_count, int split);
 
 // Workspace bytes the call below will use with these operands: 0 when it takes
-// the cluster-split strip kernel (which needs none), else the split-K kernels'
-// need for this problem.
+// the cluster-split kernel (which needs none, whatever the split), else the
+// split-K kernels' need for this problem.
 int gemv_call_workspace_bytes(const void* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
                               int64_t qz_ld, const void* s, int64_t s_ld, int M, int N, int K, int G, int split_k,
                               size_t* bytes) {
@@ -416,8 +416,8 @@ int gemv_call_workspace_bytes(const void* x, int64_t x_ld, const int32_t* qw, in
   int rc = device_info(&info);
   if (rc) return rc;
   const bool cluster_ok = gemv_cluster_eligible(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, M, N, G);
-  if (cluster_ok && (g_gemv_impl == 4 || (g_gemv_impl == 0 && split_k <= 0)) &&
-      gemv_cluster_plannable(M, N, K, G, info.sm_count)) {
+  if (cluster_ok && (g_gemv_impl == 4 || g_gemv_impl == 0) &&
+      gemv_cluster_plannable(M, N, K, G, info.sm_count, split_k)) {
     *bytes = 0;
     return ASHQK_OK;
   }
@@ -432,12 +432,13 @@ int gemv_launch_rows(const __half* x, int64_t x_ld, const int32_t* qw, int64_t q
   int rc = device_info(&info);
   if (rc) return rc;
   if (G % 16) return ASHQK_ERR_UNSUPPORTED;
-  // Column strips need no workspace; a forced split_k asks for a K split, so it
-  // goes to the split-K kernels.
+  // The cluster-split kernel takes a caller's split_k as its K split (CTAs per
+  // cluster) and needs no workspace. Column strips split K their own way, so a
+  // forced split_k that the cluster kernel cannot plan goes to the split-K kernels.
   const bool cluster_ok = gemv_cluster_eligible(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, M, N, G);
   if (g_gemv_impl == 4 && !cluster_ok) return ASHQK_ERR_UNSUPPORTED;
-  if (cluster_ok && (g_gemv_impl == 4 || (g_gemv_impl == 0 && split_k <= 0))) {
-    const int rc_cl = gemv_cluster_launch(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G,
+  if (cluster_ok && (g_gemv_impl == 4 || g_gemv_impl == 0)) {
+    const int rc_cl = gemv_cluster_launch(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G, split_k,
                                           info.sm_count, stream);
     if (!(rc_cl == ASHQK_ERR_UNSUPPORTED && g_gemv_impl == 0)) return rc_cl;
   }

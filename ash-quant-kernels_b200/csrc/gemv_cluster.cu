@@ -560,7 +560,9 @@ int groups_spanned(int stages, int R, int G) {
 
 }  // namespace
 
-bool plan_cluster(int M, int N, int K, int G, int sm_count, ClusterPlan* p) {
+// split > 0: the caller's K split (the reference's split_k): that many CTAs per cluster, at most 16 and
+// at most the tile's stages.
+bool plan_cluster(int M, int N, int K, int G, int sm_count, ClusterPlan* p, int split) {
   if (M < 1 || M > 16 || N % 32 || G % 16 || sm_count < 1) return false;
   const int toks = M == 1 ? 1 : (M <= 8 ? 8 : 16);
   const int smem_kb = g_smem_kb.load(std::memory_order_relaxed);
@@ -576,7 +578,7 @@ bool plan_cluster(int M, int N, int K, int G, int sm_count, ClusterPlan* p) {
   const int max_ctas = g_max_ctas.load(std::memory_order_relaxed) > 0
                            ? std::min(g_max_ctas.load(std::memory_order_relaxed), 2 * sm_count)
                            : (M <= 8 ? sm_count * 33 / 20 : sm_count * 13 / 20);
-  const int force_c = g_force_c.load(std::memory_order_relaxed);
+  const int force_c = split > 0 ? std::min(split, kMaxCluster) : g_force_c.load(std::memory_order_relaxed);
   const int force_w = g_force_w.load(std::memory_order_relaxed);
 
   // Estimated time in stage units (measured on B200, decode shapes): the busiest CTA's stages, x1.18
@@ -599,12 +601,13 @@ bool plan_cluster(int M, int N, int K, int G, int sm_count, ClusterPlan* p) {
         q.x_off = kStageWeightBytes;
         q.hoisted = hoisted;
         const int sz_row_bytes = (W / 256) * 512 + W / 2;
+        const int fc = split > 0 ? std::min(force_c, q.stages) : force_c;
         for (int C = 1; C <= kMaxCluster; ++C) {
-          if (force_c && C != force_c) continue;
+          if (fc && C != fc) continue;
           if (C > q.stages) break;
           q.C = C;
           q.ctas = q.tiles * C;
-          if (q.ctas > cta_cap && !(force_c || (C == 1 && q.tiles > cta_cap))) continue;
+          if (q.ctas > cta_cap && !(fc || (C == 1 && q.tiles > cta_cap))) continue;
           q.per = ceil_div(q.stages, C);
           // The partial strips this CTA stores: [ceil(strips / C)][C * blocks][64][M] fp32.
           const int strips = W / kStripCols, blocks = kConsumers / strips;
@@ -703,9 +706,9 @@ int launch_cluster_t(const ClusterMaps& maps, const ClusterArgs& args, size_t sm
 
 }  // namespace
 
-bool gemv_cluster_plannable(int M, int N, int K, int G, int sm_count) {
+bool gemv_cluster_plannable(int M, int N, int K, int G, int sm_count, int split) {
   ClusterPlan p;
-  return plan_cluster(M, N, K, G, sm_count, &p);
+  return plan_cluster(M, N, K, G, sm_count, &p, split);
 }
 
 bool gemv_cluster_eligible(const void* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
@@ -716,9 +719,9 @@ bool gemv_cluster_eligible(const void* x, int64_t x_ld, const int32_t* qw, int64
 
 int gemv_cluster_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz,
                         int64_t qz_ld, const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K,
-                        int G, int sm_count, cudaStream_t stream) {
+                        int G, int split, int sm_count, cudaStream_t stream) {
   ClusterPlan p;
-  if (!plan_cluster(M, N, K, G, sm_count, &p)) return ASHQK_ERR_UNSUPPORTED;
+  if (!plan_cluster(M, N, K, G, sm_count, &p, split)) return ASHQK_ERR_UNSUPPORTED;
   ClusterMaps maps;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(N / 8), static_cast<uint64_t>(K)};
@@ -813,7 +816,7 @@ extern "C" int ashqk_gemv_cluster_plan(int M, int N, int K, int group_size, int 
     sm_count = info.sm_count;
   }
   ashqk::ClusterPlan p;
-  if (!ashqk::plan_cluster(M, N, K, group_size, sm_count, &p)) return ASHQK_ERR_UNSUPPORTED;
+  if (!ashqk::plan_cluster(M, N, K, group_size, sm_count, &p, 0)) return ASHQK_ERR_UNSUPPORTED;
   plan->tile_cols = p.W;
   plan->stage_rows = p.R;
   plan->tiles = p.tiles;

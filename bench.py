@@ -342,18 +342,18 @@ def time_graph(graph, steps, warmup, torch, dist, world):
 
 def per_layer_gemv(stack, m, torch, reps=3):
     """Average device time of one GEMV launch per layer type (graph of 36 launches
-    over the 36 distinct weight sets, so every launch streams its weights from HBM)."""
+    over the 36 distinct weight sets, so every launch streams its weights from HBM),
+    and the same with all 36 launches on layer 0's weights (resident in L2 after the
+    first): equal times mean the kernel is not bound by DRAM."""
     from ashqk import w4a16_linear
 
-    res = {}
-    for name, n, k in LAYERS:
-        x = torch.randn(m, k, device="cuda").half()
-        w4a16_linear(x, *stack[0][name])
+    def graph_us(calls):
+        calls[0]()
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            for layer in stack:
-                w4a16_linear(x, *layer[name])
+            for c in calls:
+                c()
         for _ in range(2):
             g.replay()
         torch.cuda.synchronize()
@@ -363,10 +363,17 @@ def per_layer_gemv(stack, m, torch, reps=3):
             g.replay()
         end.record()
         torch.cuda.synchronize()
-        us = start.elapsed_time(end) * 1e3 / (reps * len(stack))
-        nbytes = w4a16_bytes(m, n, k, GROUP)
-        res[name] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1), "launch": cluster_plan(m, n, k)}
         del g
+        return start.elapsed_time(end) * 1e3 / (reps * len(calls))
+
+    res = {}
+    for name, n, k in LAYERS:
+        x = torch.randn(m, k, device="cuda").half()
+        us = graph_us([lambda w=layer[name]: w4a16_linear(x, *w) for layer in stack])
+        us_l2 = graph_us([lambda w=stack[0][name]: w4a16_linear(x, *w) for _ in stack])
+        nbytes = w4a16_bytes(m, n, k, GROUP)
+        res[name] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1), "l2_resident_us": round(us_l2, 2),
+                     "launch": cluster_plan(m, n, k)}
     return res
 
 

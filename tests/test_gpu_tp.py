@@ -6,7 +6,7 @@
 * On 2+ GPUs (skipped otherwise): one process per GPU over NCCL runs
   ``ashqk.tp`` on the tensor-parallel MLP shapes (gate_up K=8192 N=57344,
   down K=28672 N=8192) and checks every rank's result against the unsharded
-  product.
+  product, and, at M = 1 and 16, against the C oracle with the parity criterion.
 """
 
 from __future__ import annotations
@@ -112,6 +112,64 @@ def test_nccl_tensor_parallel_mlp():
 
     world = min(torch.cuda.device_count(), 8)
     mp.start_processes(_nccl_worker, args=(world, _free_port()), nprocs=world, start_method="spawn", join=True)
+
+
+def _nccl_oracle_worker(rank, world, port):
+    """Config-5 MLP layers at full size through ashqk.tp over NCCL; rank 0 checks the result of every
+    call against the C oracle (fp32 dequantisation, fp64 accumulation) with the parity criterion."""
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    layers = []
+    for name, n, k, mode in (("gate_up", 57344, 8192, "column"), ("down", 8192, 28672, "row")):
+        rng = np.random.default_rng(n + k)  # every rank builds the same layer (BASELINE distributions)
+        qw = rng.integers(0, 2 ** 32, size=(k, n // 8), dtype=np.uint32).view(np.int32)
+        qz = rng.integers(0, 2 ** 32, size=(k // 128, n // 8), dtype=np.uint32).view(np.int32)
+        s = rng.uniform(0.002, 0.02, size=(k // 128, n)).astype(np.float16)
+        x = rng.standard_normal((16, k), dtype=np.float32).astype(np.float16)
+        layers.append((name, n, k, mode, x, qw, qz, s))
+    outs = {}
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        from ashqk import tp
+
+        for name, n, k, mode, x, qw, qz, s in layers:
+            xd, qwd, qzd, sd = (torch.from_numpy(a).to(dev) for a in (x, qw, qz, s))
+            for m in (1, 16):
+                if mode == "column":
+                    y = tp.column_parallel_linear(xd[:m], *tp.shard_columns(qwd, qzd, sd, rank, world))
+                else:
+                    y = tp.row_parallel_linear(tp.shard_input(xd[:m], rank, world),
+                                               *tp.shard_rows(qwd, qzd, sd, rank, world), reduce_dtype=torch.float32)
+                outs[(name, m)] = y.float().cpu().numpy()
+            del xd, qwd, qzd, sd
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    from ashqk import _ext
+
+    for name, n, k, mode, x, qw, qz, s in layers:
+        y_true = O.c_gemm(x, qw, qz, s)
+        xd, qwd, qzd, sd = (torch.from_numpy(a).to(dev) for a in (x, qw, qz, s))
+        y_cublas = (xd @ _ext.ops().dequantize_awq(qwd, qzd, sd, torch.float16)).float().cpu().numpy()
+        for m in (1, 16):
+            e_cublas = O.rel_err(y_cublas[:m], y_true[:m])
+            e = O.rel_err(outs[(name, m)], y_true[:m])
+            assert e <= 2 * e_cublas + 1e-5, (name, mode, m, world, e, e_cublas)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2+ GPUs")
+def test_nccl_tensor_parallel_mlp_matches_oracle():
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 8)
+    mp.start_processes(_nccl_oracle_worker, args=(world, _free_port()), nprocs=world, start_method="spawn", join=True)
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])

@@ -81,7 +81,8 @@ def test_noalloc_matches_workspace_entry_point(m, n, k, g, split):
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
-    """A split forcing more than 8 MiB of partial sums is refused before any launch."""
+    """A split forcing more than 8 MiB of partial sums is refused before any launch. (The default
+    kernel takes a split without scratch, so the split-K kernel, which uses it, is forced here.)"""
     lib = _lib()
     m, n, k, g = 16, 24576, 4096, 128
     size = ctypes.c_size_t(0)
@@ -89,6 +90,10 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     assert size.value > (8 << 20)
     xd, qwd, qzd, sd = to_cuda(*O.make_problem(m, n, k, g, seed=1))
     y = torch.zeros(m, n, dtype=torch.float16, device="cuda")
-    assert _call_noalloc(lib, xd, qwd, qzd, sd, y, m, n, k, g, 32) == 3  # ASHQK_ERR_WORKSPACE
+    assert lib.ashqk_set_gemv_kernel(2) == 0
+    try:
+        assert _call_noalloc(lib, xd, qwd, qzd, sd, y, m, n, k, g, 32) == 3  # ASHQK_ERR_WORKSPACE
+    finally:
+        assert lib.ashqk_set_gemv_kernel(0) == 0
     torch.cuda.synchronize()
     assert int(y.abs().sum()) == 0  # nothing was written
