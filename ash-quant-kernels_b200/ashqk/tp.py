@@ -112,16 +112,19 @@ def column_parallel_linear(x: torch.Tensor, qweight, qzeros, scales, group=None,
 
 def row_parallel_linear(x_local: torch.Tensor, qweight, qzeros, scales, group=None,
                         reduce_dtype: Optional[torch.dtype] = None, linear: Optional[Linear] = None,
-                        allreduce: Optional["P2PAllReduce"] = None) -> torch.Tensor:
+                        allreduce: Optional["P2PAllReduce"] = None, fused: bool = False) -> torch.Tensor:
     """Partial y = x[..., shard] @ W[shard, :] on every rank, summed over ranks.
 
     ``reduce_dtype=torch.float32`` sums the partials in fp32 (one rounding to
     fp16 at the end instead of one per reduction step). ``allreduce`` (a
     ``P2PAllReduce`` of the same group) replaces NCCL for partials it can hold;
-    it too sums in fp32 with one rounding.
+    it too sums in fp32 with one rounding. ``fused=True`` with a low-latency
+    ``allreduce`` runs the GEMV and the all-reduce as one kernel where it takes
+    the shard (the column-strip GEMV with the all-reduce in its epilogue; on
+    B200 slower than the default GEMV followed by the all-reduce).
     """
     _, world = _world(group)
-    if world > 1 and linear is None and allreduce is not None and allreduce.protocol == "ll":
+    if fused and world > 1 and linear is None and allreduce is not None and allreduce.protocol == "ll":
         y = allreduce.fused_linear(x_local, qweight, qzeros, scales)
         if y is not None:  # GEMV and all-reduce in one kernel
             return y

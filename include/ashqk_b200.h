@@ -70,9 +70,11 @@ ASHQK_API int ashqk_gemv_workspace_size(int M, int N, int K, int group_size, int
 
 /*
  * Decode GEMV, 1 <= M <= ashqk_gemv_max_m(): y = x @ deq(qweight, qzeros, scales).
- * Tensor-core (mma.sync m16n8k16) dot products on register-dequantised int4,
- * per-group factored scales, split-K reduced in the same launch.
- * split_k <= 0 picks the split from the problem size and SM count.
+ * Tensor-core (mma.sync m16n8k16) dot products on int4 unpacked in registers,
+ * per-group factored scales and zero points, split-K reduced in the same launch.
+ * split_k <= 0 picks the split from the problem size and SM count; split_k > 0
+ * is the number of CTAs that share each output tile's K (at most 16), which
+ * needs no workspace when the default kernel takes the problem.
  * Replaces ashqk/kernels/w4a16_gemv.py:132-167 (w4a16_gemv).
  */
 ASHQK_API int ashqk_w4a16_gemv(const void* x, int64_t x_ld, const int32_t* qweight, int64_t qw_ld,
@@ -86,8 +88,7 @@ ASHQK_API int ashqk_w4a16_gemv(const void* x, int64_t x_ld, const int32_t* qweig
  * cannot allocate device memory (a plugin that is handed only device pointers
  * by its host framework, or a caller that must not call cudaMalloc on its hot
  * path). Calls that take the default cluster-split kernel (16-byte aligned
- * operands, N % 32 == 0, group_size % 16 == 0, no split_k) use no scratch at
- * all. The split-K kernels the other calls take use a fixed 8 MiB array inside
+ * operands, N % 32 == 0, group_size % 16 == 0) use no scratch at all. The split-K kernels the other calls take use a fixed 8 MiB array inside
  * this library, held on every GPU that loads it until the process exits;
  * those whose scratch need exceeds it return ASHQK_ERR_WORKSPACE without
  * launching anything. The first such call on a device looks up that array's
@@ -103,11 +104,12 @@ ASHQK_API int ashqk_w4a16_gemv_noalloc(const void* x, int64_t x_ld, const int32_
 
 /*
  * Selects the decode GEMV kernel for later calls in this process: 0 = automatic
- * (cluster-split column strips when N % 32 == 0, group_size % 16 == 0, rows
- * are 16-byte aligned and no split_k is requested; else the split-K TMA kernel
- * when eligible; else the register-streaming kernel), 1 = always
+ * (cluster-split tiles when N % 32 == 0, group_size % 16 == 0, rows are
+ * 16-byte aligned and a plan fits; else column strips when no split_k is
+ * requested; else the split-K TMA kernel when eligible; else the
+ * register-streaming kernel), 1 = always
  * register-streaming, 2 = always split-K TMA, 3 = always column strips over
- * the whole K per CTA, 4 = always cluster-split column strips (ineligible
+ * the whole K per CTA, 4 = always cluster-split tiles (ineligible
  * problems then return ASHQK_ERR_UNSUPPORTED). No reference counterpart: a
  * test and tuning switch.
  */

@@ -269,10 +269,11 @@ def _p2p_worker(rank, world, port, protocol="oneshot"):
 
             from ashqk import _ext, w4a16_linear
 
+            y_fused = tp.row_parallel_linear(xs, *sh, allreduce=ar, fused=True)
             lib = ctypes.CDLL(_ext.C_LIBRARY)
             assert lib.ashqk_set_gemv_kernel(3) == 0
             try:
-                assert torch.equal(y_p2p, ar(w4a16_linear(xs, *sh)))
+                assert torch.equal(y_fused, ar(w4a16_linear(xs, *sh)))
             finally:
                 assert lib.ashqk_set_gemv_kernel(0) == 0
         ar.check()
