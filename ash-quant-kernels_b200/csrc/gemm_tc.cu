@@ -460,14 +460,19 @@ int gemm_tc_pair_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_
 int gemm_tc_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_t qw_ld, const int32_t* qz, int64_t qz_ld,
                    const __half* s, int64_t s_ld, __half* y, int64_t y_ld, int M, int N, int K, int G, int sm_count,
                    cudaStream_t stream) {
-  // CTA pairs (cta_group::2) once M spans two 128-row tiles, N % 256 == 0 and
-  // the pair tiles fill most of the SM pairs: each SM then writes and feeds
-  // the tensor core half as much of the fp16 weight tile, which bounds the
-  // one-CTA kernel (shared-memory bandwidth).
+  // CTA pairs (cta_group::2) once M spans two 128-row tiles, N % 256 == 0,
+  // the pair tiles occupy at least ~0.6 of the SM pairs and padding M to 256
+  // rows wastes at most 1/8 of them: each SM then writes and feeds the tensor
+  // core half as much of the fp16 weight tile, which bounds the one-CTA kernel
+  // (shared-memory bandwidth). Measured crossover on the Qwen3-8B shapes: pairs
+  // win from 48 tiles (o, qkv, down at M = 768; qkv at 512), the one-CTA
+  // kernel below that and when M is an odd number of 128-row tiles (384).
   const bool pair_ok = gemm_tc_pair_eligible(M, N);
   const int pair_tiles = pair_ok ? ceil_div(M, 2 * kBM) * (N / 256) : 0;
+  const bool pair_fill = 10 * 2 * pair_tiles >= 6 * sm_count;
+  const bool pair_pad = 8 * ceil_div(M, 2 * kBM) * (2 * kBM) <= 9 * M;
   if (g_gemm_impl == 4 && !pair_ok) return ASHQK_ERR_UNSUPPORTED;
-  if (g_gemm_impl == 4 || (pair_ok && g_gemm_impl != 3 && 2 * pair_tiles >= sm_count))
+  if (g_gemm_impl == 4 || (pair_ok && g_gemm_impl != 3 && pair_fill && pair_pad))
     return gemm_tc_pair_launch(x, x_ld, qw, qw_ld, qz, qz_ld, s, s_ld, y, y_ld, M, N, K, G, sm_count, stream);
   // One CTA per tile: 256-column tiles unless that leaves most SMs idle and 128
   // columns divide N; with fewer tiles than half the SMs, split K over a

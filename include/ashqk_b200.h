@@ -118,7 +118,8 @@ ASHQK_API int ashqk_set_gemv_kernel(int which);
 /*
  * Selects the prefill GEMM kernel for later calls in this process: 0 = automatic
  * (tcgen05 when the problem is eligible -- on CTA pairs, cta_group::2 with
- * M = 256 per instruction, when M > 128 and N % 256 == 0, else one CTA per
+ * M = 256 per instruction, when M > 128, N % 256 == 0, the 256-row tiles fill
+ * at least ~0.6 of the SM pairs and pad M by at most 1/8, else one CTA per
  * output tile -- otherwise the chunked GEMV), 1 = always the chunked GEMV,
  * 2 = always tcgen05 (automatic variant), 3 = tcgen05 on one CTA per tile,
  * 4 = tcgen05 on CTA pairs. Forced choices return ASHQK_ERR_UNSUPPORTED for
