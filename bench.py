@@ -823,41 +823,25 @@ def run_gpu(args):
                                      k // (world if nm in ("o", "down") else 1), GROUP)
                          for nm, n, k in LAYERS) * n_layers
     stack_gbs = per_rank_bytes / (ms1 * 1e-3) / 1e9
-    # The one JSON line (stdout) stays short enough to be read whole from the end of the log;
-    # the detail (launch shapes, per-shape breakdowns, Marlin and Qwen3.5 figures) goes to stderr.
+    # The one JSON line (stdout) stays short (~1.5 KB) and ends with the figures a reader of the log's
+    # tail needs (cuBLAS and prefill comparisons, the M=4 step); the detail (launch shapes, per-layer
+    # and per-shape breakdowns, Marlin and Qwen3.5 figures) goes to stderr.
     line = {
         "metric": METRIC, "value": round(ms1 * 1e3, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": warmup, "ms_per_step": round(ms1, 4), "higher_is_better": False, "scaling": "strong",
         "vs_baseline": None, "dtype": "fp16 x int4 (AWQ), fp32 accumulate", "data": "synthetic",
         "config": workload_config(world, n_layers),
-        "m4_us_per_token": round(ms4 * 1e3 / 4, 1), "m4_us_per_step": round(ms4 * 1e3, 1),
         "stack_hbm_frac": round(stack_gbs / hbm_peak, 3),
         "gpu_launches": args.steps * len(LAYERS) * n_layers,
         "clocks": clocks.summary(),
         "e2e": {"value": round(e2e_ms * 1e3, 1), "unit": UNIT, "h2d_bytes_per_step": 4096 * 2,
-                "d2h_bytes_per_step": d2h_bytes,
-                "how": "pinned H2D of the hidden state + graph replay of the 144 w4a16_linear calls + D2H of the output"},
+                "d2h_bytes_per_step": d2h_bytes},
     }
     detail = {"device": {"name": torch.cuda.get_device_name(device),
                          "sm_count": torch.cuda.get_device_properties(device).multi_processor_count},
-              "stack_hbm_gbs_per_gpu": round(stack_gbs, 1)}
-    if cublas_us is not None:
-        line["cublas_fp16"] = {
-            "us_per_token": round(cublas_us[1], 1), "m4_us_per_step": round(cublas_us[4], 1),
-            "speedup_m1": round(cublas_us[1] / (ms1 * 1e3), 2), "speedup_m4": round(cublas_us[4] / (ms4 * 1e3), 2)}
-        detail["cublas_fp16_how"] = ("x @ W_fp16 (torch.matmul -> cuBLAS) on the dequantised weights of the same "
-                                     "stack, same chaining, CUDA graph, CUDA events")
-    if sweep is not None:
-        line["decode_sweep"] = {"layers": [nm for nm, _, _ in LAYERS], **sweep}
-    if prefill is not None:
-        detail["prefill_gemm"] = prefill
-        line["prefill_gemm"] = {"m": list(PREFILL_M), "peak_tflops": tensor_peak}
-        for nm, _, _ in PREFILL_LAYERS:
-            line["prefill_gemm"][nm] = {
-                "us": [prefill[f"{nm}_m{m}"]["us"] for m in PREFILL_M],
-                "frac": [prefill[f"{nm}_m{m}"]["frac_of_peak"] for m in PREFILL_M],
-                "cublas_frac": [round(prefill[f"{nm}_m{m}"]["cublas_fp16_tflops"] / tensor_peak, 3)
-                                for m in PREFILL_M]}
+              "stack_hbm_gbs_per_gpu": round(stack_gbs, 1),
+              "e2e_how": "pinned H2D of the hidden state + graph replay of the 144 w4a16_linear calls + D2H "
+                         "of the output, every step, CUDA events"}
     if tp_res is not None:
         detail["tp_mlp"] = tp_res
         line["tp_mlp"] = {k: [v["us"], v["frac"]] for k, v in tp_res.items()}
@@ -866,25 +850,43 @@ def run_gpu(args):
         line["qwen35_9b_us"] = [q35["m1"]["us_per_step"], q35["m4"]["us_per_step"]]
     if marlin_res is not None:
         detail["marlin_vllm"] = marlin_res
-        if "per_layer_m1_us" in marlin_res and "stack_us_per_token_est" in marlin_res:
-            line["marlin_vllm"] = {"m1_us": [marlin_res["per_layer_m1_us"].get(nm) for nm, _, _ in LAYERS],
-                                   "stack_est": marlin_res["stack_us_per_token_est"]}
+        if "stack_us_per_token_est" in marlin_res:
+            line["marlin_vllm_us"] = marlin_res["stack_us_per_token_est"]
+    if layer_bw is not None and args.cpu_seconds > 0:
+        value, threads, desc, _ = cpu_reference_sample(1000, 1, budget_s=args.cpu_seconds)
+        detail["cpu_baseline_sample"] = desc
+        line["cpu_baseline"] = {"value": round(value, 1), "unit": UNIT, "cores": threads, "kind": "port",
+                                "sample": "one decoder layer's 4 calls at M=1 via the C port of ref.py, x36"}
     if layer_bw is not None:
         tot_bytes = sum(w4a16_bytes(1, n, k, GROUP) for _, n, k in LAYERS)
         tot_us = sum(layer_bw[nm]["us"] for nm, _, _ in LAYERS)
         achieved = tot_bytes / tot_us / 1e3
         detail["per_layer_gemv"] = layer_bw
+        detail["roofline_detail"] = {"algorithmic_bytes": tot_bytes, "peak_kind": peak_kind,
+                                     "per_layer_us": [layer_bw[nm]["us"] for nm, _, _ in LAYERS],
+                                     "kernel": "gemv_cluster_kernel, M=1, one launch of each layer type"}
         line["roofline"] = {
             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-            "frac": round(achieved / hbm_peak, 3), "peak_kind": peak_kind,
-            "traffic": load_traffic(), "algorithmic_bytes": tot_bytes,
-            "per_layer_us": [layer_bw[nm]["us"] for nm, _, _ in LAYERS],
-            "kernel": "gemv_cluster_kernel, M=1, one launch of each layer type (qkv, o, gate_up, down)",
+            "frac": round(achieved / hbm_peak, 3), "traffic": load_traffic(), "kernel": "gemv_cluster_kernel",
         }
-    if layer_bw is not None and args.cpu_seconds > 0:
-        value, threads, desc, _ = cpu_reference_sample(1000, 1, budget_s=args.cpu_seconds)
-        line["cpu_baseline"] = {"value": round(value, 1), "unit": UNIT, "cores": threads, "kind": "port",
-                                "sample": desc}
+    if sweep is not None:
+        detail["decode_sweep"] = sweep
+        line["decode_sweep"] = {k: [round(sum(v["us"]), 1), v["vs_cublas"], v["frac"]] for k, v in sweep.items()}
+    if prefill is not None:
+        detail["prefill_gemm"] = prefill
+        line["prefill_gemm"] = {"m": list(PREFILL_M)}
+        for nm, _, _ in PREFILL_LAYERS:
+            line["prefill_gemm"][f"{nm}_frac"] = [prefill[f"{nm}_m{m}"]["frac_of_peak"] for m in PREFILL_M]
+            line["prefill_gemm"][f"{nm}_cublas_frac"] = [
+                round(prefill[f"{nm}_m{m}"]["cublas_fp16_tflops"] / tensor_peak, 3) for m in PREFILL_M]
+    if cublas_us is not None:
+        line["cublas_fp16"] = {
+            "us_per_token": round(cublas_us[1], 1), "m4_us_per_step": round(cublas_us[4], 1),
+            "speedup_m1": round(cublas_us[1] / (ms1 * 1e3), 2), "speedup_m4": round(cublas_us[4] / (ms4 * 1e3), 2)}
+        detail["cublas_fp16_how"] = ("x @ W_fp16 (torch.matmul -> cuBLAS) on the dequantised weights of the same "
+                                     "stack, same chaining, CUDA graph, CUDA events")
+    line["m4_us_per_token"] = round(ms4 * 1e3 / 4, 1)
+    line["m4_us_per_step"] = round(ms4 * 1e3, 1)
     print(json.dumps(detail), file=sys.stderr, flush=True)
     print(json.dumps(line), flush=True)
 
