@@ -174,6 +174,11 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def default_tp_allreduce(world):
+    """The row-parallel reduction bench.py uses without ASHQK_TP_ALLREDUCE: NVLink lines up to 4 ranks."""
+    return "ll" if world <= 4 else "nccl"
+
+
 def workload_config(world, n_layers=N_LAYERS):
     cfg = {
         "workload": "BASELINE config 3: 36-layer Qwen3-8B-shape linear stack (qkv 4096->6144, o 4096->4096, "
@@ -182,7 +187,7 @@ def workload_config(world, n_layers=N_LAYERS):
         "model": "qwen3-8b linear layers (random AWQ weights)",
         "global_batch": 1, "seq_len": 1,
         "parallelism": f"tp{world}" if world > 1 else "none",
-        "tp_allreduce": os.environ.get("ASHQK_TP_ALLREDUCE", "ll") if world > 1 else None,
+        "tp_allreduce": os.environ.get("ASHQK_TP_ALLREDUCE", default_tp_allreduce(world)) if world > 1 else None,
         "l2": "inputs larger than L2: 3.6 GB of distinct per-layer weights per step",
     }
     if n_layers != N_LAYERS:  # a reduced stack (profiling runs), not the benchmark workload
@@ -738,12 +743,13 @@ def run_gpu(args):
             print(json.dumps({"prefill": res}), flush=True)
         return
     stack = make_stack(world, rank, device, args.layers)
-    # Tensor-parallel reductions: the NVLink low-latency-line all-reduce by default (fastest on
-    # B200 at tp2: 1272 us/token against 1405 fused, 1471 one-shot p2p and 1828 NCCL);
-    # ASHQK_TP_ALLREDUCE=nccl, =p2p (one-shot) or =fused (the row-parallel GEMV and its
-    # all-reduce as one kernel, low-latency lines) select the others.
+    # Tensor-parallel reductions: the NVLink low-latency-line all-reduce by default up to 4 ranks
+    # (fastest on B200: tp2 1272 us/token against 1405 fused, 1471 one-shot p2p and 1828 NCCL; tp4
+    # 1243 against 1830 NCCL), NCCL beyond (the line protocol has not run on 8 GPUs here);
+    # ASHQK_TP_ALLREDUCE=nccl, =ll, =p2p (one-shot) or =fused (the row-parallel GEMV and its
+    # all-reduce as one kernel, low-latency lines) selects one.
     p2p = None
-    tp_reduce = os.environ.get("ASHQK_TP_ALLREDUCE", "ll")
+    tp_reduce = os.environ.get("ASHQK_TP_ALLREDUCE", default_tp_allreduce(world))
     if tp_reduce not in ("nccl", "p2p", "ll", "fused"):
         raise SystemExit(f"ASHQK_TP_ALLREDUCE={tp_reduce!r}: expected nccl, p2p, ll or fused")
     fused = world > 1 and tp_reduce == "fused"
