@@ -88,6 +88,7 @@ struct ClusterArgs {
   int sz_rows;      // rows the area holds: >= the groups its K range spans
   int sz_box_rows;  // rows per copy
   int tile_off;     // byte offset of the CTA's partial tile (outside the ring)
+  int presum;       // the blocks of a strip are added in the CTA before the exchange (else sent apart)
   int y_pairs;      // y rows allow 4-byte half2 stores
   uint32_t tx_bytes;     // per stage: weights, x (and the area when not hoisted)
   uint32_t sz_tx_bytes;  // a hoisted area
@@ -139,10 +140,10 @@ __device__ __forceinline__ void st_async_v4(uint32_t remote_addr, uint4 v, uint3
                "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(remote_bar)
                : "memory");
 }
-__device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
                : "r"(addr)
                : "memory");
   return v;
@@ -178,8 +179,9 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
   const int nloc = part_lo(rank + 1, a.stages, C) - st0;
   const int M = a.M, R = a.R, G = a.G, ring = a.ring, stage_bytes = a.stage_bytes;
   const int W = a.W, strips = W / kStripCols, blocks = kConsumers / strips;
-  const int nsend = C * blocks;  // partial strips per stored strip: CTA r, block b at slot r * blocks + b
   const int my_strips = strips > rank ? (strips - rank + C - 1) / C : 0;  // strips rank, rank + C, ...
+  // Partial strips per stored strip: one per CTA (presum) or one per (CTA, block) at slot rank * blocks + block.
+  const int nsend = a.presum ? C : C * blocks;
   // The partial strips this CTA stores: [my_strips][nsend][64 columns][M] fp32.
   float* slots = reinterpret_cast<float*>(smem + a.tile_off);
 
@@ -191,7 +193,8 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
     mbar_init(&sz_full, 1);
     mbar_init(&partials, 1);
     if (C > 1 && my_strips > 0)  // what the other CTAs will store here with st.async
-      mbar_arrive_expect_tx(&partials, static_cast<uint32_t>(my_strips * (C - 1) * blocks * kStripCols * M * 4));
+      mbar_arrive_expect_tx(&partials,
+                            static_cast<uint32_t>(my_strips * (C - 1) * (nsend / C) * kStripCols * M * 4));
     abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -465,25 +468,28 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
   }
 
   // ---------------- the cluster's sum ----------------
-  // Strip s of the tile is stored by CTA s % C of the cluster. Each consumer warp (strip, block) hands
-  // its partial strip to that CTA's slot [rank * blocks + block]; the owner adds the C * blocks slots in
-  // that fixed order and stores y. Slot layout [64 columns][M tokens] fp32. A strip owned here is
-  // stored straight from registers; one owned elsewhere is first laid out in this CTA's (consumed)
-  // ring and then sent as 16-byte st.async pieces, which complete on the owner's `partials` barrier --
-  // a quarter of the remote stores of sending single values.
+  // Strip s of the tile is stored by CTA s % C of the cluster. The consumer warps lay their partial
+  // strips out in this CTA's consumed ring ([64 columns][M tokens] fp32 each) and hand them to the
+  // owner's slots in 16-byte st.async pieces that complete on the owner's `partials` barrier (plain
+  // stores when the owner is this CTA). With presum (M > 4, where the slots would crowd out the ring)
+  // the blocks of each strip are first added here, in block order, and the CTA sends one partial per
+  // strip to slot [rank]; otherwise warp (strip, block) sends its own to slot [rank * blocks + block].
+  // The owner adds its slots in that fixed order (deterministic) and stores y.
   if (C > 1) cluster_wait_acquire();  // every CTA's `partials` barrier is armed
   if (warp < kConsumers) {
     const int strip = warp % strips, block = warp / strips;
     const int g = lane >> 2, t = lane & 3, wA = g >> 1, hA = g & 1;
     const int owner = strip % C;
-    const int sender = rank * blocks + block;
-    // this strip's slot in the owner: owned strip index strip / C
-    const uint32_t slot_base = static_cast<uint32_t>(((strip / C) * nsend + sender) * kStripCols * M * 4);
     const bool remote = owner != rank;
+    const uint32_t strip_bytes = static_cast<uint32_t>(kStripCols * M * 4);
+    const bool presum = a.presum != 0;
     // Every consumer warp is past its last stage before any of them reuses the ring.
-    if (C > 1) asm volatile("bar.sync 1, %0;" ::"r"(32 * kConsumers) : "memory");
-    const uint32_t dst = remote ? smem_u32(smem) + static_cast<uint32_t>(warp * kStripCols * M * 4)
-                                : smem_u32(slots) + slot_base;
+    if (presum || C > 1) asm volatile("bar.sync 1, %0;" ::"r"(32 * kConsumers) : "memory");
+    const uint32_t stg = smem_u32(smem);  // warp w's partial strip at stg + w * strip_bytes
+    // Without presum a strip owned here goes straight into its slot.
+    const uint32_t direct_slot = static_cast<uint32_t>((strip / C) * nsend + rank * blocks + block) * strip_bytes;
+    const uint32_t dst = (presum || remote) ? stg + static_cast<uint32_t>(warp) * strip_bytes
+                                            : smem_u32(slots) + direct_slot;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -501,11 +507,35 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
             if (TOKS > 1 && m0 + 1 < M) sts_f32(addr + 4, v1);
           }
         }
-    if (remote) {
+    const int pieces = kStripCols * M / 4;
+    if (presum) {
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * kConsumers) : "memory");  // every block's strip is laid out
+      // The warps of strip s share its 16-byte pieces: warp (s, b) adds and sends part b of blocks.
+      const int lo = part_lo(block, pieces, blocks), hi = part_lo(block + 1, pieces, blocks);
+      const uint32_t slot = static_cast<uint32_t>((strip / C) * nsend + rank) * strip_bytes;
+      const uint32_t out = remote ? map_shared_rank(slots, owner) + slot : smem_u32(slots) + slot;
+      const uint32_t bar = remote ? map_shared_rank(&partials, owner) : 0u;
+      for (int i = lo + lane; i < hi; i += 32) {
+        float4 v = lds_f4(stg + static_cast<uint32_t>(strip) * strip_bytes + 16 * i);
+        for (int b = 1; b < blocks; ++b) {
+          const float4 u = lds_f4(stg + static_cast<uint32_t>(b * strips + strip) * strip_bytes + 16 * i);
+          v.x += u.x;
+          v.y += u.y;
+          v.z += u.z;
+          v.w += u.w;
+        }
+        const uint4 bits = make_uint4(__float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z),
+                                      __float_as_uint(v.w));
+        if (remote)
+          st_async_v4(out + 16 * i, bits, bar);
+        else
+          sts_v4(out + 16 * i, bits);
+      }
+    } else if (remote) {
       __syncwarp();
-      const uint32_t rdst = map_shared_rank(slots, owner) + slot_base;
+      const uint32_t rdst = map_shared_rank(slots, owner) + direct_slot;
       const uint32_t bar = map_shared_rank(&partials, owner);
-      for (int i = lane; i < kStripCols * M / 4; i += 32) st_async_v4(rdst + 16 * i, lds_v4(dst + 16 * i), bar);
+      for (int i = lane; i < pieces; i += 32) st_async_v4(rdst + 16 * i, lds_v4(dst + 16 * i), bar);
     }
   }
   __syncthreads();  // this CTA's own strips are in its slots
@@ -611,7 +641,9 @@ bool plan_cluster(int M, int N, int K, int G, int sm_count, ClusterPlan* p, int 
           q.per = ceil_div(q.stages, C);
           // The partial strips this CTA stores: [ceil(strips / C)][C * blocks][64][M] fp32.
           const int strips = W / kStripCols, blocks = kConsumers / strips;
-          const size_t slots = static_cast<size_t>(ceil_div(strips, C)) * C * blocks * kStripCols * M * 4;
+          // presum (M > 4): one partial per CTA and strip; else one per CTA, strip and block.
+          const size_t slots =
+              static_cast<size_t>(ceil_div(strips, C)) * C * (M > 4 ? 1 : blocks) * kStripCols * M * 4;
           // The scale / zero area: the groups of the longest stage range (hoisted) or of one stage, in
           // copies of at most 256 rows.
           const int span = groups_spanned(hoisted ? q.per : 1, q.R, G);
@@ -778,6 +810,7 @@ int gemv_cluster_launch(const __half* x, int64_t x_ld, const int32_t* qw, int64_
   a.sz_box_rows = p.sz_box_rows;
   a.tile_off = p.tile_off;
   a.y_pairs = aligned(y, 4) && (y_ld % 2 == 0);
+  a.presum = M > 4 ? 1 : 0;
   a.tx_bytes = p.tx;
   a.sz_tx_bytes = p.sz_tx;
   const bool gb = G % kBlockRows == 0;
