@@ -38,6 +38,16 @@ def test_workload_config_names_the_baseline_config():
     assert b.workload_config(1, 2)["decoder_layers"] == 2
 
 
+def test_multi_gpu_default_reduction():
+    """The low-latency NVLink all-reduce where it has run on this pool's boxes (2 and 4 ranks), NCCL
+    beyond; the workload config echoes the choice."""
+    b = _bench()
+    assert [b.default_tp_allreduce(n) for n in (2, 4, 8)] == ["ll", "ll", "nccl"]
+    if "ASHQK_TP_ALLREDUCE" not in os.environ:
+        assert b.workload_config(2)["tp_allreduce"] == "ll" and b.workload_config(8)["tp_allreduce"] == "nccl"
+        assert b.workload_config(1)["tp_allreduce"] is None
+
+
 def test_qwen35_shapes_are_the_references():
     b = _bench()
     names = {n: (nn, k, c) for n, nn, k, c in b.QWEN35_LAYERS}
