@@ -39,7 +39,8 @@
 //    (1024 + q) or (1024 + 16 q) (the exponent of 1024 ORed over the nibble,
 //    csrc/awq_unpack.cuh); the zero point is not subtracted per weight;
 //  * mma.sync.m16n8k16 accumulates those against x (tokens along n), plus one
-//    mma against ones for the group's sum of x;
+//    mma against ones for the group's sum of x (at one token: one per block,
+//    its B columns the block's eight steps);
 //  * once per group: sum x (q - z) = f * dot - (c + z) * sum x, with f = 1,
 //    c = 1024 (low nibble of a byte) or f = 1/16, c = 64 (high nibble), times
 //    the scale, into the fp32 accumulator.
@@ -108,6 +109,10 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t (&r)[2]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
 }
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
@@ -291,6 +296,14 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
       return xbase + row * 32 + 16 * (xq_half ^ ((row >> 2) & 1));
     };
     const int x_off = a.x_off;
+    // One token and whole-block groups: the block's sum of x comes from one mma per stage against
+    // ones whose B column n is step n of the block (ldmatrix row n = x row n of the block, k halves
+    // as matrices 0 and 1), added over the columns afterwards, instead of an mma against ones at every
+    // step: a fifth of the tensor work, which bounds a stage when two CTAs share an SM. (With 2 or 4
+    // tokens, M such mma per block measured slower than the per-step form.)
+    constexpr bool kBlockSumX = TOKS == 1 && GB;
+    const int xs_row = block * (kBlockRows / 16) + (lane & 7);
+    const uint32_t xs_lane = static_cast<uint32_t>(xs_row * 32 + 16 * (((lane >> 3) & 1) ^ ((xs_row >> 2) & 1)));
     // Scale row r of this strip's box: (strip / 4) * sz_rows + r rows of 512 bytes; zero row r: W / 2 bytes.
     const uint32_t s_lane =
         static_cast<uint32_t>(a.sz_off + (strip >> 2) * a.sz_rows * 512 + (strip & 3) * 128);
@@ -382,12 +395,14 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
             mma_16816(part[mt][j], A, bx[mt][2 * h], bx[mt][2 * h + 1]);
         }
       }
+      if constexpr (!kBlockSumX) {
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        if (first)
-          mma_16816_first(psx[mt], ones_a, bx[mt][2 * h], bx[mt][2 * h + 1]);
-        else
-          mma_16816(psx[mt], ones_a, bx[mt][2 * h], bx[mt][2 * h + 1]);
+        for (int mt = 0; mt < MT; ++mt) {
+          if (first)
+            mma_16816_first(psx[mt], ones_a, bx[mt][2 * h], bx[mt][2 * h + 1]);
+          else
+            mma_16816(psx[mt], ones_a, bx[mt][2 * h], bx[mt][2 * h + 1]);
+        }
       }
     };
     // Whole-block groups (G % 128 == 0): fold the block's sums into acc with its group's scale and
@@ -431,12 +446,14 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
       }
       const uint32_t wbase = base + w_lane;
       const uint32_t xbase = base + x_off;
-      // Loads run one step pair ahead of the arithmetic.
-      uint32_t bx[MT][4], Ra[4], Rb[4];
+      // Loads run one step pair ahead of the arithmetic; the block's x rows for its sum of x load with
+      // the first pair and their mma follows that pair's steps.
+      uint32_t bx[MT][4], Ra[4], Rb[4], bs[2];
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) ldsm_x4(x_addr(xbase, 0, mt), bx[mt]);
       ldsm_x4_trans(wbase, Ra);
       ldsm_x4_trans(wbase + kStepBytes, Rb);
+      if constexpr (kBlockSumX) ldsm_x2(xbase + xs_lane, bs);
 #pragma unroll
       for (int s = 0; s < kBlockRows / 16; s += 2) {
         uint32_t bxn[MT][4], Ran[4], Rbn[4];
@@ -450,6 +467,7 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
         step(Ra, bx, 0, GB && s == 0);
         if (!GB) enter_group(kb + 16 * (s + 1));
         step(Rb, bx, 1, false);
+        if (kBlockSumX && s == 0) mma_16816_first(psx[0], ones_a, bs[0], bs[1]);  // column n: step n's sum
         if (s + 2 < kBlockRows / 16) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -459,6 +477,12 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), TOKS > 8 ? 1 : 2)
             for (int mt = 0; mt < MT; ++mt) bx[mt][i] = bxn[mt][i];
           }
         }
+      }
+      if constexpr (kBlockSumX) {  // lane (g, t) holds steps 2t and 2t + 1
+        float v = psx[0][0] + psx[0][1];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        psx[0][0] = v;
       }
       if (GB) fold_block(kb / G - g_ref);
       __syncwarp();

@@ -226,3 +226,34 @@ def test_planted_errors_are_caught():
     for kw in ({"nibble_shift_bug": True}, {"swizzle_reads": False}):
         y = emulate_strip(qw.view(np.uint32), qz.view(np.uint32), s, x, 128, **kw)
         assert not np.allclose(y, y_true, rtol=1e-3), kw
+
+
+def emulate_block_sums(x, half_bug=False):
+    """The one-token kernel's sum of x over a 128-row block: one ldmatrix.x2 of the block's 8 x rows
+    (lanes 0-7 give the rows of matrix 0 = k 0-7, lanes 8-15 those of matrix 1 = k 8-15, the 32-byte
+    swizzle applied), one mma against ones (B column n = step n), then the kernel's lane shuffles.
+    Returns each lane's value."""
+    st = Stage(np.zeros((ROWS, WORDS), dtype=np.uint32), x.astype(np.float16).view(np.uint16)[:, :ROWS], 1)
+    mats = []
+    for q in range(2):  # lane 8 q + r gives row r of matrix q
+        half = 0 if half_bug else q
+        mats.append([st.row16(st.x, r * 32 + 16 * (half ^ ((r >> 2) & 1))) for r in range(8)])
+    regs = ldsm_x4(mats + mats, trans=False)
+    B = np.zeros((16, 8))
+    for lane in range(32):
+        g, t = lane >> 2, lane & 3
+        B[2 * t, g], B[2 * t + 1, g] = halves(regs[lane][0])
+        B[2 * t + 8, g], B[2 * t + 9, g] = halves(regs[lane][1])
+    D = np.ones((16, 16)) @ B
+    v = np.array([D[lane >> 2, 2 * (lane & 3)] + D[lane >> 2, 2 * (lane & 3) + 1] for lane in range(32)])
+    for mask in (1, 2):
+        v = v + v[[lane ^ mask for lane in range(32)]]
+    return v
+
+
+def test_block_sum_of_x():
+    """Every lane ends with the block's sum of x; a planted error (matrix 1 reading k 0-7) fails."""
+    x = np.random.default_rng(3).standard_normal((1, ROWS)).astype(np.float16)
+    want = float(x.astype(np.float64).sum())
+    assert np.allclose(emulate_block_sums(x), want, rtol=0, atol=1e-9)
+    assert not np.allclose(emulate_block_sums(x, half_bug=True), want, rtol=1e-3)
